@@ -1,0 +1,374 @@
+#!/usr/bin/env python
+"""LTHC interface benchmark on B200 (one JSON line on rank 0).
+
+Step = one fused materialisation X_L = X_0 + sum_{l<12} P_l(dZ_l) over one batch
+of BASELINE configuration 2 (B=64 per GPU, bf16 activations, fp32 write weights,
+NHWC [64, 64, 64, 768] residual, 12 workspace updates [64, 256, 768]).  The
+metric is algorithmic HBM bytes per second (1,107,886,080 B per step and GPU),
+summed over GPUs (weak scaling: every rank runs its own batch, no collective on
+the data path).  Inputs are 1.1 GB per step, larger than the 126 MB L2, so no L2
+flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the CPU restatement of the reference's algorithm
+(``oracle/``, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+from flowmatching_lthc_b200 import dist as D  # noqa: E402
+from flowmatching_lthc_b200 import workloads as W  # noqa: E402
+
+METRIC = "LTHC read/write/materialise HBM GB/s vs peak"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+B_DEFAULT, G, C, L = 64, 16, 768, 12
+TRAFFIC_FILE = ROOT / "profiles" / "materialise_fwd_b64_bf16.md"
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=B_DEFAULT, help="images per GPU (BASELINE config 2: 64)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
+    p.add_argument("--no-extras", action="store_true", help="skip the per-kernel and comparator measurements")
+    return p.parse_args()
+
+
+def hbm_peak() -> tuple[float, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_launch() -> float | None:
+    """dram bytes (read + write) per materialise launch at the bench config, from the
+    committed ncu summary (line 'dram_bytes_per_launch: N')."""
+    try:
+        for line in TRAFFIC_FILE.read_text().splitlines():
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except Exception:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, interval_ms: int = 100):
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        exe = shutil.which("nvidia-smi")
+        if not exe:
+            return
+        self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      f"-lms={interval_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                     text=True)
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [s.strip() for s in line.split(",")]))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(2)
+
+    def summary(self, t0: float, t1: float, gpus: int) -> dict:
+        rows = [s for t, s in self.samples if t0 <= t <= t1 and len(s) >= 9]
+        note = None
+        if not rows:
+            rows = [s for _, s in self.samples if len(s) >= 9]
+            note = "no sample fell inside the timed region; all samples of the run"
+        rows = [s for s in rows if s[0].isdigit() and int(s[0]) < gpus]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+        sm = [float(s[1]) for s in rows if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in rows if s[2].replace(".", "").isdigit()]
+        reasons = sorted({name for s in rows for name, v in zip(self.REASONS, s[5:9]) if v.lower() == "active"})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": reasons, "samples": len(rows)}
+        if note:
+            out["note"] = note
+        return out
+
+
+# ------------------------------------------------------------------ helpers
+def time_device(fn, iters: int, stream: torch.cuda.Stream) -> float:
+    """Average device time in ms of fn() over `iters` calls (CUDA events on `stream`)."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(iters):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The oracle (CPU restatement of the reference's algorithm) on a bounded
+    sample of the same workload, all host threads."""
+    from oracle import lthc_oracle as O
+
+    Bs = 4
+    cfg = W.config2(B=Bs, seed=0)
+    O.materialise(cfg["x0"], cfg["dz"], cfg["P"])
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.materialise(cfg["x0"], cfg["dz"], cfg["P"])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    by = W.materialise_bytes(Bs, G, C, L, 2) * n
+    return {"value": round(by / el / 1e9, 4), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n} x materialise of B={Bs} (config 2 shapes, bf16) in {el:.1f} s on {O.num_threads()} threads"}
+
+
+# ------------------------------------------------------------------ reference arm
+def reference_arm(args, r: D.Rank) -> int:
+    if not r.is_main:
+        return 0
+    from oracle import lthc_oracle as O
+
+    per_step_s = 0.035  # measured B=4 cost of the oracle materialisation on 8 cores
+    Bs = 4 if (args.steps + args.warmup) * per_step_s <= 120 else 1
+    cfg = W.config2(B=Bs, seed=0)
+    for _ in range(max(args.warmup, 1)):
+        O.materialise(cfg["x0"], cfg["dz"], cfg["P"])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.materialise(cfg["x0"], cfg["dz"], cfg["P"])
+    el = time.perf_counter() - t0
+    by = W.materialise_bytes(Bs, G, C, L, 2)
+    value = by * args.steps / el / 1e9
+    sample = (f"each step: oracle materialise of B={Bs} of config 2 (bf16 in/out, fp32 weights), "
+              f"{O.num_threads()} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": r.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) residual, N(0,0.1) updates, N(0,0.02) weights)",
+        "config": config_dict(args.batch, r.world),
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(B: int, world: int) -> dict:
+    return {"workload": "materialise fwd X_L = X_0 + sum_l P_l(dZ_l), BASELINE config 2",
+            "global_batch": B * world, "batch_per_gpu": B, "residual": [B, 4 * G, 4 * G, C],
+            "updates": [L, B, G * G, C], "act_dtype": "bf16", "weight_dtype": "fp32",
+            "parallelism": f"dp{world} (batch-sharded replicas, no data-path collective)",
+            "l2": "inputs 1.1 GB per step per GPU > 126 MB L2; no flush needed"}
+
+
+# ------------------------------------------------------------------ our arm
+def main() -> int:
+    args = parse_args()
+    r = D.from_env()
+    if args.impl == "reference":
+        return reference_arm(args, r)
+
+    from flowmatching_lthc_b200 import ops
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(r.local_rank)
+    dev = torch.device("cuda", r.local_rank)
+    D.init("nccl", r)
+    stream = torch.cuda.current_stream(dev)
+    B = args.batch
+
+    cfg = W.config2(B=B, device=dev, seed=1000 + r.rank)
+    x0, dz, P = cfg["x0"], cfg["dz"], cfg["P"]
+    step = lambda: ops.materialise(x0, dz, P)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler() if r.is_main else None
+    time.sleep(0.3 if sampler else 0)
+    D.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    D.barrier()
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms_local = ev0.elapsed_time(ev1)
+    ms = D.reduce_max(ms_local, dev)
+    if sampler:
+        sampler.stop()
+    clocks = sampler.summary(t_wall0, t_wall1, r.world) if sampler else None
+
+    bytes_step = W.materialise_bytes(B, G, C, L, 2)
+    value = r.world * bytes_step * args.steps / (ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    kernel_ms = ms_local / args.steps  # one materialise launch per step
+    achieved = bytes_step / (kernel_ms / 1e3) / 1e9
+    traffic = ncu_traffic_per_launch()
+    if traffic is not None and B != B_DEFAULT:
+        traffic *= B / B_DEFAULT
+
+    # end to end through the public operator: pinned host inputs -> device -> host result
+    e2e = None
+    extras = {}
+    if r.is_main or r.world > 1:
+        h_x0 = x0.cpu().pin_memory()
+        h_dz = [d.cpu().pin_memory() for d in dz]
+        h_out = torch.empty_like(h_x0).pin_memory()
+        d_x0 = torch.empty_like(x0)
+        d_dz = [torch.empty_like(d) for d in dz]
+
+        def e2e_step():
+            d_x0.copy_(h_x0, non_blocking=True)
+            for a, b in zip(d_dz, h_dz):
+                a.copy_(b, non_blocking=True)
+            out = ops.materialise(d_x0, d_dz, P)
+            h_out.copy_(out, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        n_e2e = max(3, min(args.steps, 10))
+        e2e_ms = time_device(e2e_step, n_e2e, stream)
+        e2e_ms = D.reduce_max(e2e_ms, dev)
+        h2d = h_x0.numel() * 2 + sum(d.numel() * 2 for d in h_dz)
+        e2e = {"value": round(r.world * bytes_step / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h_out.numel() * 2,
+               "ms_per_step": round(e2e_ms, 3), "steps": n_e2e,
+               "path": "pinned host buffers -> cudaMemcpyAsync -> lthc_b200::materialise (C ABI) -> host"}
+        del h_x0, h_dz, h_out, d_x0, d_dz
+
+    if r.world == 1 and not args.no_extras:
+        extras = measure_kernels(B, dev, stream, x0, dz, P, peak)
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": r.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) residual, N(0,0.1) updates, N(0,0.02) fp32 weights; no dataset)",
+        "config": config_dict(B, r.world),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "lthc::broadcast_kernel (materialise fwd)", "algorithmic_bytes_per_launch": bytes_step},
+        "cpu_baseline": None,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if extras:
+        line["kernels"] = extras.get("kernels")
+        line["comparators"] = extras.get("comparators")
+    if r.is_main and r.world == 1:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if r.is_main:
+        print(json.dumps(line), flush=True)
+    D.barrier()
+    D.shutdown()
+    return 0
+
+
+def measure_kernels(B, dev, stream, x0, dz, P, peak) -> dict:
+    """Device-timed GB/s of every LTHC kernel at B=64 bf16 (informational; not the
+    headline), plus the reference's Triton ops on the same inputs when the
+    reference package is installed under baseline/_ref."""
+    from flowmatching_lthc_b200 import ops
+
+    out: dict = {"kernels": {}, "comparators": {}}
+    iters = 20
+    alpha = torch.softmax(torch.randn(C, 16, device=dev), -1).to(torch.bfloat16)
+    g = W.residual(B, G, C, seed=7, device=dev, dtype=torch.bfloat16)
+    z = torch.randn(B, G * G, C, device=dev, dtype=torch.bfloat16)
+    beta_bf = P[0].to(torch.bfloat16)
+
+    def rec(name, fn, nbytes, launches):
+        fn()
+        ms = time_device(fn, iters, stream)
+        out["kernels"][name] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                                "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4), "bytes": nbytes,
+                                "launches": launches}
+
+    rec("materialise_fwd", lambda: ops.materialise(x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1)
+    rec("materialise_bwd", lambda: ops.materialise_bwd(g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2),
+        3)
+    rec("read_fwd", lambda: ops.read(x0, alpha), W.read_bytes(B, G, C, 2, 2), 1)
+    rec("write_add_fwd", lambda: ops.write_add(x0, dz[0], beta_bf), W.write_add_bytes(B, G, C, 2, 2), 1)
+    rec("lazy_update_fwd", lambda: ops.lazy_update(z, dz[0], alpha, beta_bf), W.lazy_bytes(B * G * G, C, 2, 2), 1)
+    rec("read_bwd", lambda: ops.read_bwd(x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3)
+    rec("lazy_update_bwd", lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta_bf), W.lazy_bytes(B * G * G, C, 2, 2), 2)
+
+    ref = ROOT / "baseline" / "_ref"
+    if (ref / "flowmatching_lthc").exists():
+        try:
+            sys.path.insert(0, str(ref))
+            import flowmatching_lthc.models.local_thc  # noqa: F401  (registers jit_thc:: ops)
+
+            f = torch.ops.jit_thc.final_accumulate_b4_12_traceable
+            fn = lambda: f(x0, *dz, *P)  # noqa: E731
+            fn()
+            ms = time_device(fn, iters, stream)
+            nb = W.materialise_bytes(B, G, C, L, 2)
+            out["comparators"]["triton_final_accumulate_b4_12"] = {
+                "ms": round(ms, 4), "gbs": round(nb / (ms / 1e3) / 1e9, 1),
+                "speedup_of_ours": round(ms / out["kernels"]["materialise_fwd"]["ms"], 3)}
+            gdz_op = torch.ops.jit_thc.final_accumulate_b4_12_grad_dz_ptr
+            gb_op = torch.ops.jit_thc.final_accumulate_b4_12_grad_beta_ptr
+            fnb = lambda: (gdz_op(g, *P), gb_op(g, *dz))  # noqa: E731
+            fnb()
+            ms = time_device(fnb, iters, stream)
+            nb = W.materialise_bwd_bytes(B, G, C, L, 2)
+            out["comparators"]["triton_final_accumulate_b4_12_bwd"] = {
+                "ms": round(ms, 4), "gbs": round(nb / (ms / 1e3) / 1e9, 1),
+                "speedup_of_ours": round(ms / out["kernels"]["materialise_bwd"]["ms"], 3)}
+        except Exception as e:  # the reference's own Triton path
+            out["comparators"]["error"] = f"{type(e).__name__}: {str(e)[:200]}"
+    else:
+        out["comparators"]["note"] = "reference package not installed under baseline/_ref"
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

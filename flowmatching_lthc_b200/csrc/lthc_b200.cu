@@ -1,0 +1,618 @@
+// C ABI of the LTHC kernels: argument validation, grid sizing and dtype/depth
+// dispatch.  The library never allocates device memory; scratch for the
+// two-stage weight-gradient reductions is passed in by the caller.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "lthc_b200.h"
+#include "lthc_common.cuh"
+#include "lthc_kernels.cuh"
+
+namespace lthc {
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// Device-side error word (bounded waits that gave up, refused indices).
+__device__ int g_device_error = 0;
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool ok = false;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+// Returns LTHC_OK and fills *sms for the current device, or LTHC_ERR_DEVICE.
+int current_device(int* sms) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return fail(LTHC_ERR_DEVICE, "no current CUDA device");
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.ok) {
+      int sm = 0, major = 0;
+      if (cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(LTHC_ERR_DEVICE, "cannot query CUDA device %d", dev);
+      }
+      d.sms = sm;
+      d.major = major;
+      d.ok = true;
+    }
+    if (d.major != 10) return fail(LTHC_ERR_DEVICE, "device %d is sm_%d0, this library is built for sm_100a", dev, d.major);
+    *sms = d.sms;
+  }
+  return LTHC_OK;
+}
+
+// SM count used for grid sizing in workspace queries; falls back to the B200
+// count when no device is current (the query then only over-estimates).
+int sms_for_sizing() {
+  int sms = 0;
+  if (current_device(&sms) != LTHC_OK) {
+    g_last_error[0] = '\0';
+    return 148;
+  }
+  return sms;
+}
+
+bool valid_act(int dt) { return dt == LTHC_DTYPE_F32 || dt == LTHC_DTYPE_BF16 || dt == LTHC_DTYPE_F16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_geometry(int64_t B, int64_t G, int64_t C, int act_dtype) {
+  if (B < 0) return fail(LTHC_ERR_SHAPE, "batch must be >= 0, got %lld", (long long)B);
+  if (G < 1 || G > 4096) return fail(LTHC_ERR_SHAPE, "workspace grid must be in [1, 4096], got %lld", (long long)G);
+  if (C < 8 || C > 16384 || C % 8 != 0)
+    return fail(LTHC_ERR_SHAPE, "channels must be a multiple of 8 in [8, 16384], got %lld", (long long)C);
+  if (!valid_act(act_dtype)) return fail(LTHC_ERR_DTYPE, "unknown activation dtype code %d", act_dtype);
+  return LTHC_OK;
+}
+
+int check_ptr(const void* p, const char* name) {
+  if (!p) return fail(LTHC_ERR_NULL_POINTER, "%s is NULL", name);
+  if (!aligned16(p)) return fail(LTHC_ERR_ALIGNMENT, "%s is not 16-byte aligned", name);
+  return LTHC_OK;
+}
+
+int check_layers(int L) {
+  if (L < 1 || L > kMaxLayers) return fail(LTHC_ERR_SHAPE, "n_layers must be in [1, %d], got %d", kMaxLayers, L);
+  return LTHC_OK;
+}
+
+int launched(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(LTHC_ERR_LAUNCH, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return LTHC_OK;
+}
+
+#define LTHC_TRY(expr)           \
+  do {                           \
+    int _st = (expr);            \
+    if (_st != LTHC_OK) return _st; \
+  } while (0)
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t slices_of(int64_t C) { return ceil_div(C, kSliceCh); }
+
+// ---- grid plans (pure functions of the problem size and the SM count) ------
+struct CellPlan {
+  int64_t blocks_x;
+  int64_t cells_per_block;
+};
+
+// CTAs that each walk a contiguous range of cells; about `per_sm` CTAs per SM.
+CellPlan plan_cells(int64_t cells, int64_t C, int sms, int per_sm, int64_t min_cells) {
+  const int64_t slices = slices_of(C);
+  int64_t bx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
+  bx = std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(cells, min_cells)));
+  const int64_t cpb = ceil_div(cells, bx);
+  return CellPlan{ceil_div(cells, cpb), cpb};
+}
+
+CellPlan plan_wgrad(int64_t cells, int64_t C, int sms) { return plan_cells(cells, C, sms, 4, 16); }
+
+int64_t plan_grid_stride(int64_t rows, int64_t C, int sms, int per_sm, int rows_per_block) {
+  const int64_t slices = slices_of(C);
+  int64_t bx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
+  return std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(rows, rows_per_block)));
+}
+
+size_t wgrad_ws_bytes(int64_t cells, int64_t C, int L, int sms) {
+  if (cells <= 0) return 0;
+  const CellPlan pl = plan_wgrad(cells, C, sms);
+  return static_cast<size_t>(pl.blocks_x) * L * C * kPos * sizeof(float);
+}
+
+size_t lazy_ws_bytes(int64_t N, int64_t C, int sms) {
+  if (N <= 0) return 0;
+  return static_cast<size_t>(plan_grid_stride(N, C, sms, 4, kLazyWarps)) * C * sizeof(float);
+}
+
+// ---- dispatch helpers -----------------------------------------------------
+template <typename T>
+int launch_broadcast(BroadcastParams p, int L, bool has_base, int sms, cudaStream_t s) {
+  const CellPlan pl = plan_cells(p.cells, p.C, sms, 8, 4);
+  p.cells_per_block = pl.cells_per_block;
+  dim3 grid(static_cast<unsigned>(pl.blocks_x), static_cast<unsigned>(slices_of(p.C)));
+  if (L == 1) {
+    if (has_base) broadcast_kernel<T, 1, true><<<grid, 128, 0, s>>>(p);
+    else broadcast_kernel<T, 1, false><<<grid, 128, 0, s>>>(p);
+  } else if (L == 12) {
+    if (has_base) broadcast_kernel<T, 12, true><<<grid, 128, 0, s>>>(p);
+    else broadcast_kernel<T, 12, false><<<grid, 128, 0, s>>>(p);
+  } else {
+    if (has_base) broadcast_kernel<T, 0, true><<<grid, 128, 0, s>>>(p);
+    else broadcast_kernel<T, 0, false><<<grid, 128, 0, s>>>(p);
+  }
+  return launched("broadcast");
+}
+
+int broadcast(BroadcastParams p, int L, bool has_base, int act, cudaStream_t s) {
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  switch (act) {
+    case LTHC_DTYPE_F32: return launch_broadcast<float>(p, L, has_base, sms, s);
+    case LTHC_DTYPE_BF16: return launch_broadcast<__nv_bfloat16>(p, L, has_base, sms, s);
+    default: return launch_broadcast<__half>(p, L, has_base, sms, s);
+  }
+}
+
+template <typename T>
+int launch_pool1(const PoolParams& p, int sms, cudaStream_t s) {
+  const int64_t bx = plan_grid_stride(p.cells, p.C, sms, 8, kPoolWarps);
+  dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(slices_of(p.C)));
+  pool1_kernel<T><<<grid, 32 * kPoolWarps, 0, s>>>(p);
+  return launched("read");
+}
+
+template <typename T, int LT>
+int launch_pool_multi_t(const PoolMultiParams& p, int sms, cudaStream_t s) {
+  constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
+  const size_t smem = sizeof(float2) * kPos * LMAX * 32;
+  static_assert(sizeof(float2) * kPos * LMAX * 32 <= 48 * 1024, "weight slice must fit the default 48 KB");
+  const int64_t bx = plan_grid_stride(p.cells, p.C, sms, 4, kPoolWarps);
+  dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(slices_of(p.C)));
+  pool_multi_kernel<T, LT><<<grid, 32 * kPoolWarps, smem, s>>>(p);
+  return launched("read (multi-layer)");
+}
+
+template <typename T>
+int launch_pool_multi(const PoolMultiParams& p, int sms, cudaStream_t s) {
+  if (p.L == 12) return launch_pool_multi_t<T, 12>(p, sms, s);
+  if (p.L == 1) return launch_pool_multi_t<T, 1>(p, sms, s);
+  return launch_pool_multi_t<T, 0>(p, sms, s);
+}
+
+template <typename T>
+int launch_wgrad(WgradParams p, float* out, int sms, cudaStream_t s) {
+  const CellPlan pl = plan_wgrad(p.cells, p.C, sms);
+  p.cells_per_block = pl.cells_per_block;
+  dim3 grid(static_cast<unsigned>(pl.blocks_x), static_cast<unsigned>(slices_of(p.C)));
+  if (p.L == 12) wgrad_kernel<T, 12><<<grid, 128, 0, s>>>(p);
+  else if (p.L == 1) wgrad_kernel<T, 1><<<grid, 128, 0, s>>>(p);
+  else wgrad_kernel<T, 0><<<grid, 128, 0, s>>>(p);
+  LTHC_TRY(launched("weight-grad"));
+  const int64_t n = static_cast<int64_t>(p.L) * p.C * kPos;
+  const int64_t rb = std::min<int64_t>(ceil_div(n, 256), static_cast<int64_t>(sms) * 8);
+  reduce_partials_kernel<<<static_cast<unsigned>(rb), 256, 0, s>>>(p.partial, out, n, static_cast<int>(pl.blocks_x));
+  return launched("weight-grad reduce");
+}
+
+int weight_grad_impl(const void* high, const void* const* low, int L, float* grad_w, void* ws, size_t ws_bytes,
+                     int64_t B, int64_t G, int64_t C, int act, cudaStream_t s) {
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  const int64_t cells = B * G * G;
+  if (cells == 0) {
+    // Empty batch: the gradient is exactly zero.
+    if (cudaMemsetAsync(grad_w, 0, sizeof(float) * L * C * kPos, s) != cudaSuccess) return launched("memset");
+    return LTHC_OK;
+  }
+  const size_t need = wgrad_ws_bytes(cells, C, L, sms);
+  if (!ws || ws_bytes < need)
+    return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
+  if (!aligned16(ws)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+  WgradParams p{};
+  p.high = high;
+  for (int l = 0; l < L; ++l) p.low[l] = low[l];
+  p.partial = static_cast<float*>(ws);
+  p.L = L;
+  p.G = static_cast<int>(G);
+  p.C = C;
+  p.cells = cells;
+  switch (act) {
+    case LTHC_DTYPE_F32: return launch_wgrad<float>(p, grad_w, sms, s);
+    case LTHC_DTYPE_BF16: return launch_wgrad<__nv_bfloat16>(p, grad_w, sms, s);
+    default: return launch_wgrad<__half>(p, grad_w, sms, s);
+  }
+}
+
+int pool_multi_impl(const void* x, const void* const* w, int w_dtype, int L, void* const* out, int64_t B,
+                    int64_t G, int64_t C, int act, cudaStream_t s) {
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  PoolMultiParams p{};
+  p.x = x;
+  for (int l = 0; l < L; ++l) {
+    p.w[l] = w[l];
+    p.out[l] = out[l];
+  }
+  p.w_dtype = w_dtype;
+  p.L = L;
+  p.G = static_cast<int>(G);
+  p.C = C;
+  p.cells = B * G * G;
+  if (p.cells == 0) return LTHC_OK;
+  if (L == 1) {
+    PoolParams q{x, w[0], out[0], w_dtype, static_cast<int>(G), C, p.cells};
+    switch (act) {
+      case LTHC_DTYPE_F32: return launch_pool1<float>(q, sms, s);
+      case LTHC_DTYPE_BF16: return launch_pool1<__nv_bfloat16>(q, sms, s);
+      default: return launch_pool1<__half>(q, sms, s);
+    }
+  }
+  switch (act) {
+    case LTHC_DTYPE_F32: return launch_pool_multi<float>(p, sms, s);
+    case LTHC_DTYPE_BF16: return launch_pool_multi<__nv_bfloat16>(p, sms, s);
+    default: return launch_pool_multi<__half>(p, sms, s);
+  }
+}
+
+int check_weight_dtype(int dt, const char* name) {
+  if (!valid_act(dt)) return fail(LTHC_ERR_DTYPE, "unknown %s dtype code %d", name, dt);
+  return LTHC_OK;
+}
+
+}  // namespace
+}  // namespace lthc
+
+using namespace lthc;
+
+extern "C" {
+
+int lthc_version(void) { return 100; }
+
+const char* lthc_status_string(int status) {
+  switch (status) {
+    case LTHC_OK: return "ok";
+    case LTHC_ERR_NULL_POINTER: return "null pointer";
+    case LTHC_ERR_SHAPE: return "unsupported shape";
+    case LTHC_ERR_DTYPE: return "unsupported dtype";
+    case LTHC_ERR_ALIGNMENT: return "misaligned pointer";
+    case LTHC_ERR_WORKSPACE: return "workspace too small";
+    case LTHC_ERR_LAUNCH: return "kernel launch failed";
+    case LTHC_ERR_DEVICE: return "no usable sm_100 device";
+    case LTHC_ERR_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* lthc_last_error_message(void) { return g_last_error; }
+
+int lthc_device_status(int* status_out, void* stream) {
+  if (!status_out) return fail(LTHC_ERR_NULL_POINTER, "status_out is NULL");
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&host, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return launched("device status read");
+  *status_out = host ? LTHC_ERR_TIMEOUT : LTHC_OK;
+  return LTHC_OK;
+}
+
+// ------------------------------ write family ---------------------------------
+
+int lthc_write_fwd(const void* dz, const void* beta, int beta_dtype, void* out, int64_t B, int64_t G, int64_t C,
+                   int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
+  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  LTHC_TRY(check_ptr(out, "out"));
+  if (B == 0) return LTHC_OK;
+  BroadcastParams p{};
+  p.base = nullptr;
+  p.dz[0] = dz;
+  p.w[0] = beta;
+  p.out = out;
+  p.w_dtype = beta_dtype;
+  p.L = 1;
+  p.G = static_cast<int>(G);
+  p.C = C;
+  p.cells = B * G * G;
+  return broadcast(p, 1, false, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int lthc_write_add_fwd(const void* x, const void* dz, const void* beta, int beta_dtype, void* out, int64_t B,
+                       int64_t G, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
+  LTHC_TRY(check_ptr(x, "x"));
+  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  LTHC_TRY(check_ptr(out, "out"));
+  if (B == 0) return LTHC_OK;
+  BroadcastParams p{};
+  p.base = x;
+  p.dz[0] = dz;
+  p.w[0] = beta;
+  p.out = out;
+  p.w_dtype = beta_dtype;
+  p.L = 1;
+  p.G = static_cast<int>(G);
+  p.C = C;
+  p.cells = B * G * G;
+  return broadcast(p, 1, true, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int lthc_materialise_fwd(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype,
+                         int n_layers, void* out, int64_t B, int64_t G, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
+  LTHC_TRY(check_layers(n_layers));
+  if (!dz || !beta) return fail(LTHC_ERR_NULL_POINTER, "dz / beta pointer arrays are NULL");
+  if (x0) LTHC_TRY(check_ptr(x0, "x0"));
+  LTHC_TRY(check_ptr(out, "out"));
+  for (int l = 0; l < n_layers; ++l) {
+    LTHC_TRY(check_ptr(dz[l], "dz[l]"));
+    LTHC_TRY(check_ptr(beta[l], "beta[l]"));
+  }
+  if (B == 0) return LTHC_OK;
+  BroadcastParams p{};
+  p.base = x0;
+  for (int l = 0; l < n_layers; ++l) {
+    p.dz[l] = dz[l];
+    p.w[l] = beta[l];
+  }
+  p.out = out;
+  p.w_dtype = beta_dtype;
+  p.L = n_layers;
+  p.G = static_cast<int>(G);
+  p.C = C;
+  p.cells = B * G * G;
+  return broadcast(p, n_layers, x0 != nullptr, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int lthc_materialise12_fwd(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype,
+                           void* out, int64_t B, int64_t G, int64_t C, int act_dtype, void* stream) {
+  return lthc_materialise_fwd(x0, dz, beta, beta_dtype, 12, out, B, G, C, act_dtype, stream);
+}
+
+size_t lthc_materialise_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C, int n_layers) {
+  if (B <= 0 || G <= 0 || C <= 0 || n_layers < 1 || n_layers > kMaxLayers) return 0;
+  return wgrad_ws_bytes(B * G * G, C, n_layers, sms_for_sizing());
+}
+
+int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void* const* beta, int beta_dtype,
+                         int n_layers, void* const* grad_dz, float* grad_beta, void* workspace,
+                         size_t workspace_bytes, int64_t B, int64_t G, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
+  LTHC_TRY(check_layers(n_layers));
+  LTHC_TRY(check_ptr(grad_out, "grad_out"));
+  if (!grad_dz && !grad_beta) return LTHC_OK;
+  if (grad_dz) {
+    if (!beta) return fail(LTHC_ERR_NULL_POINTER, "beta pointer array is NULL");
+    for (int l = 0; l < n_layers; ++l) {
+      LTHC_TRY(check_ptr(beta[l], "beta[l]"));
+      LTHC_TRY(check_ptr(grad_dz[l], "grad_dz[l]"));
+    }
+  }
+  if (grad_beta) {
+    if (!dz) return fail(LTHC_ERR_NULL_POINTER, "dz pointer array is NULL");
+    LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
+    for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_ptr(dz[l], "dz[l]"));
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (grad_beta) {
+    int sms = 0;
+    LTHC_TRY(current_device(&sms));
+    const size_t need = wgrad_ws_bytes(B * G * G, C, n_layers, sms);
+    if (B > 0 && (!workspace || workspace_bytes < need))
+      return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                  need);
+  }
+  if (grad_dz && B > 0) LTHC_TRY(pool_multi_impl(grad_out, beta, beta_dtype, n_layers, grad_dz, B, G, C, act_dtype, s));
+  if (grad_beta)
+    LTHC_TRY(weight_grad_impl(grad_out, dz, n_layers, grad_beta, workspace, workspace_bytes, B, G, C, act_dtype, s));
+  return LTHC_OK;
+}
+
+size_t lthc_write_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
+  return lthc_materialise_bwd_workspace_bytes(B, G, C, 1);
+}
+
+int lthc_write_bwd(const void* grad_out, const void* dz, const void* beta, int beta_dtype, void* grad_dz,
+                   float* grad_beta, void* workspace, size_t workspace_bytes, int64_t B, int64_t G, int64_t C,
+                   int act_dtype, void* stream) {
+  const void* dzs[1] = {dz};
+  const void* betas[1] = {beta};
+  void* gdzs[1] = {grad_dz};
+  return lthc_materialise_bwd(grad_out, dzs, betas, beta_dtype, 1, grad_dz ? gdzs : nullptr, grad_beta, workspace,
+                              workspace_bytes, B, G, C, act_dtype, stream);
+}
+
+// ------------------------------ read family ----------------------------------
+
+int lthc_read_fwd(const void* x, const void* alpha, int alpha_dtype, void* z, int64_t B, int64_t G, int64_t C,
+                  int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(alpha_dtype, "alpha"));
+  LTHC_TRY(check_ptr(x, "x"));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  LTHC_TRY(check_ptr(z, "z"));
+  if (B == 0) return LTHC_OK;
+  const void* w[1] = {alpha};
+  void* out[1] = {z};
+  return pool_multi_impl(x, w, alpha_dtype, 1, out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
+size_t lthc_weight_grad_workspace_bytes(int64_t B, int64_t G, int64_t C, int n_layers) {
+  return lthc_materialise_bwd_workspace_bytes(B, G, C, n_layers);
+}
+
+int lthc_weight_grad(const void* high, const void* const* low, int n_layers, float* grad_w, void* workspace,
+                     size_t workspace_bytes, int64_t B, int64_t G, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_layers(n_layers));
+  LTHC_TRY(check_ptr(high, "high"));
+  LTHC_TRY(check_ptr(grad_w, "grad_w"));
+  if (!low) return fail(LTHC_ERR_NULL_POINTER, "low pointer array is NULL");
+  for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_ptr(low[l], "low[l]"));
+  return weight_grad_impl(high, low, n_layers, grad_w, workspace, workspace_bytes, B, G, C, act_dtype,
+                          static_cast<cudaStream_t>(stream));
+}
+
+size_t lthc_read_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
+  return lthc_materialise_bwd_workspace_bytes(B, G, C, 1);
+}
+
+int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alpha_dtype, const void* grad_x_in,
+                  void* grad_x, float* grad_alpha, void* workspace, size_t workspace_bytes, int64_t B, int64_t G,
+                  int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_weight_dtype(alpha_dtype, "alpha"));
+  LTHC_TRY(check_ptr(grad_z, "grad_z"));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  if (grad_x_in) LTHC_TRY(check_ptr(grad_x_in, "grad_x_in"));
+  if (grad_alpha) LTHC_TRY(check_ptr(x, "x"));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (grad_alpha) {
+    int sms = 0;
+    LTHC_TRY(current_device(&sms));
+    const size_t need = wgrad_ws_bytes(B * G * G, C, 1, sms);
+    if (B > 0 && (!workspace || workspace_bytes < need))
+      return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                  need);
+  }
+  if (grad_x) {
+    LTHC_TRY(check_ptr(grad_x, "grad_x"));
+    if (B > 0) {
+      BroadcastParams p{};
+      p.base = grad_x_in;
+      p.dz[0] = grad_z;
+      p.w[0] = alpha;
+      p.out = grad_x;
+      p.w_dtype = alpha_dtype;
+      p.L = 1;
+      p.G = static_cast<int>(G);
+      p.C = C;
+      p.cells = B * G * G;
+      LTHC_TRY(broadcast(p, 1, grad_x_in != nullptr, act_dtype, s));
+    }
+  }
+  if (grad_alpha) {
+    const void* low[1] = {grad_z};
+    LTHC_TRY(weight_grad_impl(x, low, 1, grad_alpha, workspace, workspace_bytes, B, G, C, act_dtype, s));
+  }
+  return LTHC_OK;
+}
+
+// ------------------------------ lazy recurrence ------------------------------
+
+static int check_lazy(int64_t N, int64_t C, int act_dtype, int a_dtype, int b_dtype) {
+  if (N < 0) return fail(LTHC_ERR_SHAPE, "rows must be >= 0, got %lld", (long long)N);
+  if (C < 8 || C > 16384 || C % 8 != 0)
+    return fail(LTHC_ERR_SHAPE, "channels must be a multiple of 8 in [8, 16384], got %lld", (long long)C);
+  if (!valid_act(act_dtype)) return fail(LTHC_ERR_DTYPE, "unknown activation dtype code %d", act_dtype);
+  LTHC_TRY(check_weight_dtype(a_dtype, "alpha"));
+  LTHC_TRY(check_weight_dtype(b_dtype, "beta"));
+  return LTHC_OK;
+}
+
+int lthc_lazy_update_fwd(const void* z, const void* dz, const void* alpha, int alpha_dtype, const void* beta,
+                         int beta_dtype, void* z_out, int64_t N, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_lazy(N, C, act_dtype, alpha_dtype, beta_dtype));
+  LTHC_TRY(check_ptr(z, "z"));
+  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  LTHC_TRY(check_ptr(z_out, "z_out"));
+  if (N == 0) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  LazyParams p{z, dz, alpha, beta, z_out, nullptr, alpha_dtype, beta_dtype, N, C};
+  dim3 grid(static_cast<unsigned>(plan_grid_stride(N, C, sms, 4, kLazyWarps)), static_cast<unsigned>(slices_of(C)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (act_dtype) {
+    case LTHC_DTYPE_F32: lazy_fwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    case LTHC_DTYPE_BF16: lazy_fwd_kernel<__nv_bfloat16><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    default: lazy_fwd_kernel<__half><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+  }
+  return launched("lazy update");
+}
+
+size_t lthc_lazy_update_bwd_workspace_bytes(int64_t N, int64_t C) {
+  if (N <= 0 || C <= 0) return 0;
+  return lazy_ws_bytes(N, C, sms_for_sizing());
+}
+
+int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alpha, int alpha_dtype,
+                         const void* beta, int beta_dtype, void* grad_dz, float* grad_alpha, float* grad_beta,
+                         void* workspace, size_t workspace_bytes, int64_t N, int64_t C, int act_dtype,
+                         void* stream) {
+  LTHC_TRY(check_lazy(N, C, act_dtype, alpha_dtype, beta_dtype));
+  LTHC_TRY(check_ptr(grad_z_out, "grad_z_out"));
+  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  LTHC_TRY(check_ptr(grad_dz, "grad_dz"));
+  if (grad_alpha) LTHC_TRY(check_ptr(grad_alpha, "grad_alpha"));
+  if (grad_beta) LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    if (grad_alpha && cudaMemsetAsync(grad_alpha, 0, sizeof(float) * C * kPos, s) != cudaSuccess)
+      return launched("memset");
+    if (grad_beta && cudaMemsetAsync(grad_beta, 0, sizeof(float) * C * kPos, s) != cudaSuccess)
+      return launched("memset");
+    return LTHC_OK;
+  }
+  const size_t need = lazy_ws_bytes(N, C, sms);
+  if (!workspace || workspace_bytes < need)
+    return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                need);
+  if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+  const int64_t nblk = plan_grid_stride(N, C, sms, 4, kLazyWarps);
+  LazyParams p{grad_z_out, dz, alpha, beta, grad_dz, static_cast<float*>(workspace), alpha_dtype, beta_dtype, N, C};
+  dim3 grid(static_cast<unsigned>(nblk), static_cast<unsigned>(slices_of(C)));
+  switch (act_dtype) {
+    case LTHC_DTYPE_F32: lazy_bwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    case LTHC_DTYPE_BF16: lazy_bwd_kernel<__nv_bfloat16><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    default: lazy_bwd_kernel<__half><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+  }
+  LTHC_TRY(launched("lazy update backward"));
+  if (grad_alpha || grad_beta) {
+    const int64_t n = C * kPos;
+    lazy_bwd_finalize_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(p, static_cast<int>(nblk),
+                                                                                      grad_alpha, grad_beta);
+    LTHC_TRY(launched("lazy update backward finalize"));
+  }
+  return LTHC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+"""Data-parallel plumbing for the LTHC path: one process per GPU, the batch split
+into contiguous per-rank shards, no collective on the data path.  The only
+cross-rank steps are the max-over-ranks reduction of device timings (benchmark)
+and, in training, the gradient all-reduce that DDP performs on the LTHC weights
+(their gradients are sums over the batch, so per-rank sums add up exactly to
+the full-batch gradient)."""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class Rank:
+    rank: int
+    world: int
+    local_rank: int
+
+    @property
+    def is_main(self) -> bool:
+        return self.rank == 0
+
+
+def from_env() -> Rank:
+    """Read RANK / WORLD_SIZE / LOCAL_RANK as set by torch.distributed.run."""
+    return Rank(int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+                int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def init(backend: str, r: Rank, timeout_s: float = 120.0) -> None:
+    """Initialise the default process group (no-op for a single rank)."""
+    if r.world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group(backend, rank=r.rank, world_size=r.world, timeout=timedelta(seconds=timeout_s))
+
+
+def shard(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous [start, stop) of `total` items for `rank`; sizes differ by at most one."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def reduce_max(value: float, device: torch.device | str = "cpu") -> float:
+    """Max of a scalar over all ranks (identity without a process group)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum_(t: torch.Tensor) -> torch.Tensor:
+    """In-place sum over ranks (identity without a process group)."""
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t
+
+
+def barrier() -> None:
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def shutdown() -> None:
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()

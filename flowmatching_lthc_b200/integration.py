@@ -1,0 +1,133 @@
+"""Drop-in installation of the B200 kernels behind an existing ``flowmatching_lthc``.
+
+    import flowmatching_lthc.models.local_thc            # the user's reference package
+    from flowmatching_lthc_b200 import integration
+    handle = integration.install()                        # patches the LTHC methods
+    model = build_model("lthc_b4_velocity").cuda()        # unchanged API, keys, signatures
+    ...
+    handle.uninstall()                                    # restores the original methods
+
+Patched methods (``flowmatching_lthc/models/local_thc.py``):
+
+  SharedLocalRead.read                                           :1211-1223
+  LayerLocalWrite.write / write_add                              :1261-1276
+  SharedReadLocalTHCSharedAdaLNJiTBlock.lazy_workspace_update    :1325-1328
+  SharedReadLocalTHCSharedAdaLNJiT.final_accumulate_reference    :1368-1372 (pure-torch loop)
+  SharedReadFusedFinalLocalTHCSharedAdaLNJiT.final_accumulate_reference   :1407-1410 (stacked op)
+  SharedReadFusedFinal12LocalTHCSharedAdaLNJiT.final_accumulate_reference :1416-1420 (released op)
+
+Shape checks and messages are the reference's own; the arithmetic runs in
+``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
+raises); call ``uninstall()`` to get the original eager code back.
+"""
+from __future__ import annotations
+
+import importlib
+from dataclasses import dataclass, field
+from types import ModuleType
+
+import torch
+
+from . import ops
+from .modules import per_channel
+
+
+def _read(self, x: torch.Tensor) -> torch.Tensor:
+    b, h, w, c = x.shape
+    hh = self.high_grid
+    if h != hh or w != hh or c != self.hidden_size:
+        raise ValueError(f"expected [B,{hh},{hh},{self.hidden_size}], got {tuple(x.shape)}")
+    return ops.read(x, per_channel(self.alpha(dtype=x.dtype), self.hidden_size))
+
+
+def _check_dz(self, dz: torch.Tensor) -> None:
+    b, n, c = dz.shape
+    gw = self.workspace_grid
+    if n != gw * gw or c != self.hidden_size:
+        raise ValueError(f"expected [B,{gw * gw},{self.hidden_size}], got {tuple(dz.shape)}")
+
+
+def _write(self, dz: torch.Tensor) -> torch.Tensor:
+    _check_dz(self, dz)
+    return ops.write(dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+
+
+def _write_add(self, x_hi: torch.Tensor, dz: torch.Tensor) -> torch.Tensor:
+    _check_dz(self, dz)
+    return ops.write_add(x_hi, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+
+
+def _lazy_workspace_update(self, z: torch.Tensor, dz: torch.Tensor, shared_read) -> torch.Tensor:
+    alpha = shared_read.alpha(dtype=dz.dtype)
+    beta = self.write.beta(dtype=alpha.dtype)
+    c = z.shape[-1]
+    return ops.lazy_update(z, dz, per_channel(alpha, c), per_channel(beta, c))
+
+
+def _final_loop(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
+    # the pure-torch loop casts each beta to the update dtype (write_add)
+    betas = [per_channel(b.write.beta(dtype=d.dtype), x0.shape[-1]) for b, d in zip(self.blocks, dz_list, strict=True)]
+    return ops.materialise(x0, list(dz_list), betas)
+
+
+def _final_stacked(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
+    betas = [per_channel(b.write.write_weight, x0.shape[-1]) for b in self.blocks]
+    if len(dz_list) != len(betas):
+        raise ValueError(f"got {len(dz_list)} workspace updates for {len(betas)} blocks")
+    return ops.materialise(x0, list(dz_list), betas)
+
+
+def _final12(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
+    if len(dz_list) != 12 or len(self.blocks) != 12:
+        raise ValueError("SharedReadFusedFinal12LocalTHCSharedAdaLNJiT requires depth=12")
+    betas = [per_channel(b.write.write_weight, x0.shape[-1]) for b in self.blocks]
+    return ops.materialise(x0, list(dz_list), betas)
+
+
+PATCHES = (
+    ("SharedLocalRead", "read", _read),
+    ("LayerLocalWrite", "write", _write),
+    ("LayerLocalWrite", "write_add", _write_add),
+    ("SharedReadLocalTHCSharedAdaLNJiTBlock", "lazy_workspace_update", _lazy_workspace_update),
+    ("SharedReadLocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final_loop),
+    ("SharedReadFusedFinalLocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final_stacked),
+    ("SharedReadFusedFinal12LocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final12),
+)
+
+
+@dataclass
+class Installation:
+    module: ModuleType
+    saved: list = field(default_factory=list)
+
+    def uninstall(self) -> None:
+        for cls, name, had, fn in reversed(self.saved):
+            if had:
+                setattr(cls, name, fn)
+            else:
+                delattr(cls, name)
+        self.saved.clear()
+
+    def __enter__(self) -> "Installation":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.uninstall()
+
+
+def install(local_thc: ModuleType | None = None) -> Installation:
+    """Route the reference model's LTHC methods through the B200 kernels."""
+    if local_thc is None:
+        local_thc = importlib.import_module("flowmatching_lthc.models.local_thc")
+    inst = Installation(local_thc)
+    for cls_name, meth, fn in PATCHES:
+        cls = getattr(local_thc, cls_name, None)
+        if cls is None:
+            continue
+        had = meth in cls.__dict__
+        inst.saved.append((cls, meth, had, cls.__dict__.get(meth)))
+        setattr(cls, meth, fn)
+    return inst
+
+
+__all__ = ["install", "Installation", "PATCHES"]

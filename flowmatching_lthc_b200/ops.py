@@ -1,0 +1,524 @@
+"""PyTorch operators over the C-ABI CUDA library.
+
+Each operator is a ``torch.library.custom_op`` in the ``lthc_b200`` namespace with
+a CUDA implementation (a call into ``liblthc_b200.so`` on the current stream), a
+fake implementation for ``torch.compile`` tracing and an autograd formula whose
+backward is itself a custom op.  Outputs and scratch come from the PyTorch
+caching allocator; the library never allocates.  Only CUDA tensors are
+accepted: there is no CPU implementation and no fallback.
+
+The bottom of the file mirrors the reference's ``jit_thc::`` Triton op surface
+(``flowmatching_lthc/models/local_thc_triton_kernels.py``) with the same names,
+argument order and legacy read/write naming, so code written against those ops
+can switch by changing its import.
+"""
+from __future__ import annotations
+
+import math
+from typing import Sequence
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
+MAX_LAYERS = 12
+
+
+# ---------------------------------------------------------------------------
+# validation helpers (ValueError, as the reference ops raise on bad shapes,
+# e.g. local_thc_triton_kernels.py:1387-1390)
+# ---------------------------------------------------------------------------
+def _code(t: Tensor, what: str) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"{what}: unsupported dtype {t.dtype} (float32, bfloat16 or float16)") from None
+
+
+def _require_cuda(*ts: Tensor) -> None:
+    for t in ts:
+        if t.device.type != "cuda":
+            raise ValueError(f"LTHC ops run on CUDA tensors only (got a {t.device} tensor); there is no CPU path")
+
+
+def _hi_geom(x: Tensor, what: str) -> tuple[int, int, int]:
+    if x.dim() != 4:
+        raise ValueError(f"{what}: expected NHWC [B,H,W,C], got {tuple(x.shape)}")
+    b, h, w, c = x.shape
+    if h != w or h % 4 != 0:
+        raise ValueError(f"{what}: expected a square residual grid divisible by 4, got {tuple(x.shape)}")
+    _check_channels(c, what)
+    return b, h // 4, c
+
+
+def _lo_geom(z: Tensor, what: str) -> tuple[int, int, int]:
+    if z.dim() != 3:
+        raise ValueError(f"{what}: expected workspace [B,N,C], got {tuple(z.shape)}")
+    b, n, c = z.shape
+    g = math.isqrt(n)
+    if g * g != n or g == 0:
+        raise ValueError(f"{what}: workspace token count {n} is not a non-zero square")
+    _check_channels(c, what)
+    return b, g, c
+
+
+def _check_channels(c: int, what: str) -> None:
+    if c % 8 != 0 or c < 8:
+        raise ValueError(f"{what}: channel count {c} must be a positive multiple of 8")
+
+
+def _check_weight(w: Tensor, c: int, what: str) -> None:
+    if tuple(w.shape) != (c, 16):
+        raise ValueError(f"{what}: expected weight [{c},16], got {tuple(w.shape)}")
+
+
+def _stream(t: Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _workspace(nbytes: int, device: torch.device) -> Tensor:
+    # 16-byte aligned (the caching allocator returns 512-byte aligned blocks)
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def _p(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# read: residual [B,4G,4G,C] -> workspace [B,G*G,C]
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("lthc_b200::read", mutates_args=(), device_types="cuda")
+def read(x: Tensor, alpha: Tensor) -> Tensor:
+    """z[b,cell,c] = sum_r alpha[c,r] x[b,cell,r,c]  (SharedLocalRead.read, local_thc.py:1211-1223)."""
+    _require_cuda(x, alpha)
+    b, g, c = _hi_geom(x, "read")
+    _check_weight(alpha, c, "read")
+    x, alpha = x.contiguous(), alpha.contiguous()
+    z = torch.empty((b, g * g, c), device=x.device, dtype=x.dtype)
+    with torch.cuda.device(x.device):
+        _lib.call("lthc_read_fwd", x.data_ptr(), alpha.data_ptr(), _code(alpha, "read"), z.data_ptr(), b, g, c,
+                  _code(x, "read"), _stream(x))
+    return z
+
+
+@read.register_fake
+def _(x: Tensor, alpha: Tensor) -> Tensor:
+    b, h, _, c = x.shape
+    return x.new_empty((b, (h // 4) * (h // 4), c))
+
+
+@torch.library.custom_op("lthc_b200::read_bwd", mutates_args=(), device_types="cuda")
+def read_bwd(x: Tensor, grad_z: Tensor, alpha: Tensor, need_grad_x: bool, need_grad_alpha: bool) -> tuple[Tensor, Tensor]:
+    """grad_x = alpha (.) grad_z broadcast; grad_alpha = sum x*grad_z (fp32 [C,16])."""
+    _require_cuda(x, grad_z, alpha)
+    b, g, c = _hi_geom(x, "read_bwd")
+    x, grad_z, alpha = x.contiguous(), grad_z.contiguous(), alpha.contiguous()
+    gx = torch.empty_like(x) if need_grad_x else x.new_empty((0,))
+    ga = torch.empty((c, 16), device=x.device, dtype=torch.float32) if need_grad_alpha else x.new_empty((0,),
+                                                                                                      dtype=torch.float32)
+    with torch.cuda.device(x.device):
+        ws_bytes = _lib.load().lthc_read_bwd_workspace_bytes(b, g, c) if need_grad_alpha else 0
+        ws = _workspace(ws_bytes, x.device) if need_grad_alpha else None
+        _lib.call("lthc_read_bwd", x.data_ptr(), grad_z.data_ptr(), alpha.data_ptr(), _code(alpha, "read_bwd"), None,
+                  gx.data_ptr() if need_grad_x else None, ga.data_ptr() if need_grad_alpha else None, _p(ws), ws_bytes,
+                  b, g, c, _code(x, "read_bwd"), _stream(x))
+    return gx, ga
+
+
+@read_bwd.register_fake
+def _(x, grad_z, alpha, need_grad_x, need_grad_alpha):
+    c = x.shape[-1]
+    gx = torch.empty_like(x) if need_grad_x else x.new_empty((0,))
+    ga = x.new_empty((c, 16), dtype=torch.float32) if need_grad_alpha else x.new_empty((0,), dtype=torch.float32)
+    return gx, ga
+
+
+def _read_setup(ctx, inputs, output):
+    x, alpha = inputs
+    ctx.save_for_backward(x, alpha)
+
+
+def _read_backward(ctx, grad_z):
+    x, alpha = ctx.saved_tensors
+    need_x, need_a = ctx.needs_input_grad
+    if not (need_x or need_a):
+        return None, None
+    gx, ga = read_bwd(x, grad_z, alpha, need_x, need_a)
+    return (gx if need_x else None), (ga.to(alpha.dtype) if need_a else None)
+
+
+read.register_autograd(_read_backward, setup_context=_read_setup)
+
+
+# ---------------------------------------------------------------------------
+# write / write_add / materialise: workspace -> residual
+# ---------------------------------------------------------------------------
+def _materialise_impl(x0: Tensor | None, dz: Sequence[Tensor], beta: Sequence[Tensor]) -> Tensor:
+    L = len(dz)
+    if L < 1 or L > MAX_LAYERS or len(beta) != L:
+        raise ValueError(f"materialise: need 1..{MAX_LAYERS} layers with one beta each, got {L} dz / {len(beta)} beta")
+    _require_cuda(*dz, *beta)
+    b, g, c = _lo_geom(dz[0], "materialise")
+    act = dz[0].dtype
+    for t in dz:
+        if tuple(t.shape) != (b, g * g, c):
+            raise ValueError(f"materialise: every dz must be [{b},{g * g},{c}], got {tuple(t.shape)}")
+    for w in beta:
+        _check_weight(w, c, "materialise")
+    wdt = beta[0].dtype
+    dz = [t.to(act).contiguous() for t in dz]
+    beta = [w.to(wdt).contiguous() for w in beta]
+    if x0 is not None:
+        _require_cuda(x0)
+        if tuple(x0.shape) != (b, 4 * g, 4 * g, c):
+            raise ValueError(f"materialise: expected x0 [{b},{4 * g},{4 * g},{c}], got {tuple(x0.shape)}")
+        x0 = x0.to(act).contiguous()
+    out = torch.empty((b, 4 * g, 4 * g, c), device=dz[0].device, dtype=act)
+    with torch.cuda.device(out.device):
+        _lib.call("lthc_materialise_fwd", _p(x0), _lib.ptr_array([t.data_ptr() for t in dz]),
+                  _lib.ptr_array([w.data_ptr() for w in beta]), _code(beta[0], "materialise"), L, out.data_ptr(), b, g,
+                  c, _code(out, "materialise"), _stream(out))
+    return out
+
+
+@torch.library.custom_op("lthc_b200::materialise", mutates_args=(), device_types="cuda")
+def materialise(x0: Tensor, dz: list[Tensor], beta: list[Tensor]) -> Tensor:
+    """X_L = X_0 + sum_l beta_l (.) dz_l in one pass, fp32 accumulation, one rounding.
+
+    The B200 replacement of jit_thc::final_accumulate_b4_12_traceable
+    (local_thc_triton_kernels.py:1669-1736).  Output dtype = x0 dtype."""
+    if x0.dtype != dz[0].dtype:
+        dz = [t.to(x0.dtype) for t in dz]
+    return _materialise_impl(x0, dz, beta)
+
+
+@materialise.register_fake
+def _(x0, dz, beta):
+    return torch.empty_like(x0)
+
+
+@torch.library.custom_op("lthc_b200::materialise_bwd", mutates_args=(), device_types="cuda")
+def materialise_bwd(grad_out: Tensor, dz: list[Tensor], beta: list[Tensor], need_grad_dz: bool,
+                    need_grad_beta: bool) -> tuple[list[Tensor], Tensor]:
+    """grad_dz_l = sum_r beta_l grad_out (per cell); grad_beta = [L,C,16] fp32 sum grad_out*dz_l."""
+    L = len(dz)
+    _require_cuda(grad_out, *dz, *beta)
+    b, g, c = _hi_geom(grad_out, "materialise_bwd")
+    grad_out = grad_out.contiguous()
+    act = grad_out.dtype
+    dz = [t.to(act).contiguous() for t in dz]
+    beta = [w.to(beta[0].dtype).contiguous() for w in beta]
+    gdz = [torch.empty((b, g * g, c), device=grad_out.device, dtype=act) for _ in range(L)] if need_grad_dz else []
+    gbeta = (torch.empty((L, c, 16), device=grad_out.device, dtype=torch.float32) if need_grad_beta
+             else grad_out.new_empty((0,), dtype=torch.float32))
+    with torch.cuda.device(grad_out.device):
+        ws_bytes = _lib.load().lthc_materialise_bwd_workspace_bytes(b, g, c, L) if need_grad_beta else 0
+        ws = _workspace(ws_bytes, grad_out.device) if need_grad_beta else None
+        _lib.call("lthc_materialise_bwd", grad_out.data_ptr(), _lib.ptr_array([t.data_ptr() for t in dz]),
+                  _lib.ptr_array([w.data_ptr() for w in beta]), _code(beta[0], "materialise_bwd"), L,
+                  _lib.ptr_array([t.data_ptr() for t in gdz]) if need_grad_dz else None,
+                  gbeta.data_ptr() if need_grad_beta else None, _p(ws), ws_bytes, b, g, c,
+                  _code(grad_out, "materialise_bwd"), _stream(grad_out))
+    return gdz, gbeta
+
+
+@materialise_bwd.register_fake
+def _(grad_out, dz, beta, need_grad_dz, need_grad_beta):
+    b, h, _, c = grad_out.shape
+    g = h // 4
+    gdz = [grad_out.new_empty((b, g * g, c)) for _ in dz] if need_grad_dz else []
+    gbeta = (grad_out.new_empty((len(dz), c, 16), dtype=torch.float32) if need_grad_beta
+             else grad_out.new_empty((0,), dtype=torch.float32))
+    return gdz, gbeta
+
+
+def _materialise_setup(ctx, inputs, output):
+    x0, dz, beta = inputs
+    ctx.save_for_backward(*dz, *beta)
+    ctx.n_layers = len(dz)
+    ctx.x0_dtype = x0.dtype
+
+
+def _materialise_backward(ctx, grad_out):
+    L = ctx.n_layers
+    saved = ctx.saved_tensors
+    dz, beta = list(saved[:L]), list(saved[L:])
+    need_x0, need_dz, need_beta = ctx.needs_input_grad
+    grad_out = grad_out.contiguous()
+    gdz, gbeta = materialise_bwd(grad_out, dz, beta, bool(need_dz), bool(need_beta))
+    # grad_x0 aliases grad_out, as _backward_final_accumulate_12 does
+    # (local_thc_triton_kernels.py:1912)
+    grad_dz = [t.to(d.dtype) for t, d in zip(gdz, dz)] if need_dz else None
+    grad_beta = [gbeta[l].to(beta[l].dtype) for l in range(L)] if need_beta else None
+    return (grad_out if need_x0 else None), grad_dz, grad_beta
+
+
+materialise.register_autograd(_materialise_backward, setup_context=_materialise_setup)
+
+
+@torch.library.custom_op("lthc_b200::write", mutates_args=(), device_types="cuda")
+def write(dz: Tensor, beta: Tensor) -> Tensor:
+    """out[b,cell,r,c] = beta[c,r] dz[b,cell,c]  (LayerLocalWrite.write, local_thc.py:1261-1273)."""
+    _require_cuda(dz, beta)
+    b, g, c = _lo_geom(dz, "write")
+    _check_weight(beta, c, "write")
+    dz, beta = dz.contiguous(), beta.contiguous()
+    out = torch.empty((b, 4 * g, 4 * g, c), device=dz.device, dtype=dz.dtype)
+    with torch.cuda.device(dz.device):
+        _lib.call("lthc_write_fwd", dz.data_ptr(), beta.data_ptr(), _code(beta, "write"), out.data_ptr(), b, g, c,
+                  _code(dz, "write"), _stream(dz))
+    return out
+
+
+@write.register_fake
+def _(dz, beta):
+    b, n, c = dz.shape
+    g = math.isqrt(n)
+    return dz.new_empty((b, 4 * g, 4 * g, c))
+
+
+@torch.library.custom_op("lthc_b200::write_bwd", mutates_args=(), device_types="cuda")
+def write_bwd(grad_out: Tensor, dz: Tensor, beta: Tensor, need_grad_dz: bool, need_grad_beta: bool) -> tuple[Tensor, Tensor]:
+    """grad_dz = sum_r beta grad_out (per cell); grad_beta = sum grad_out*dz (fp32 [C,16])."""
+    _require_cuda(grad_out, dz, beta)
+    b, g, c = _hi_geom(grad_out, "write_bwd")
+    grad_out, dz, beta = grad_out.contiguous(), dz.to(grad_out.dtype).contiguous(), beta.contiguous()
+    gdz = torch.empty((b, g * g, c), device=dz.device, dtype=grad_out.dtype) if need_grad_dz else dz.new_empty((0,))
+    gb = (torch.empty((c, 16), device=dz.device, dtype=torch.float32) if need_grad_beta
+          else dz.new_empty((0,), dtype=torch.float32))
+    with torch.cuda.device(dz.device):
+        ws_bytes = _lib.load().lthc_write_bwd_workspace_bytes(b, g, c) if need_grad_beta else 0
+        ws = _workspace(ws_bytes, dz.device) if need_grad_beta else None
+        _lib.call("lthc_write_bwd", grad_out.data_ptr(), dz.data_ptr(), beta.data_ptr(), _code(beta, "write_bwd"),
+                  gdz.data_ptr() if need_grad_dz else None, gb.data_ptr() if need_grad_beta else None, _p(ws),
+                  ws_bytes, b, g, c, _code(grad_out, "write_bwd"), _stream(grad_out))
+    return gdz, gb
+
+
+@write_bwd.register_fake
+def _(grad_out, dz, beta, need_grad_dz, need_grad_beta):
+    c = grad_out.shape[-1]
+    gdz = torch.empty_like(dz, dtype=grad_out.dtype) if need_grad_dz else dz.new_empty((0,))
+    gb = dz.new_empty((c, 16), dtype=torch.float32) if need_grad_beta else dz.new_empty((0,), dtype=torch.float32)
+    return gdz, gb
+
+
+def _write_setup(ctx, inputs, output):
+    dz, beta = inputs
+    ctx.save_for_backward(dz, beta)
+
+
+def _write_backward(ctx, grad_out):
+    dz, beta = ctx.saved_tensors
+    need_dz, need_beta = ctx.needs_input_grad
+    if not (need_dz or need_beta):
+        return None, None
+    gdz, gb = write_bwd(grad_out, dz, beta, need_dz, need_beta)
+    return (gdz.to(dz.dtype) if need_dz else None), (gb.to(beta.dtype) if need_beta else None)
+
+
+write.register_autograd(_write_backward, setup_context=_write_setup)
+
+
+@torch.library.custom_op("lthc_b200::write_add", mutates_args=(), device_types="cuda")
+def write_add(x_hi: Tensor, dz: Tensor, beta: Tensor) -> Tensor:
+    """x_hi + write(dz)  (LayerLocalWrite.write_add, local_thc.py:1275-1276); fp32 sum, one rounding."""
+    _require_cuda(x_hi, dz, beta)
+    b, g, c = _hi_geom(x_hi, "write_add")
+    if tuple(dz.shape) != (b, g * g, c):
+        raise ValueError(f"write_add: expected dz [{b},{g * g},{c}], got {tuple(dz.shape)}")
+    _check_weight(beta, c, "write_add")
+    x_hi, dz, beta = x_hi.contiguous(), dz.to(x_hi.dtype).contiguous(), beta.contiguous()
+    out = torch.empty_like(x_hi)
+    with torch.cuda.device(x_hi.device):
+        _lib.call("lthc_write_add_fwd", x_hi.data_ptr(), dz.data_ptr(), beta.data_ptr(), _code(beta, "write_add"),
+                  out.data_ptr(), b, g, c, _code(x_hi, "write_add"), _stream(x_hi))
+    return out
+
+
+@write_add.register_fake
+def _(x_hi, dz, beta):
+    return torch.empty_like(x_hi)
+
+
+def _write_add_setup(ctx, inputs, output):
+    x_hi, dz, beta = inputs
+    ctx.save_for_backward(dz, beta)
+
+
+def _write_add_backward(ctx, grad_out):
+    dz, beta = ctx.saved_tensors
+    need_x, need_dz, need_beta = ctx.needs_input_grad
+    gdz = gb = None
+    if need_dz or need_beta:
+        gdz, gb = write_bwd(grad_out, dz, beta, need_dz, need_beta)
+    return ((grad_out if need_x else None), (gdz.to(dz.dtype) if need_dz else None),
+            (gb.to(beta.dtype) if need_beta else None))
+
+
+write_add.register_autograd(_write_add_backward, setup_context=_write_add_setup)
+
+
+# ---------------------------------------------------------------------------
+# lazy shared-read recurrence  z' = z + gamma (.) dz,  gamma = sum_r alpha*beta
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("lthc_b200::lazy_update", mutates_args=(), device_types="cuda")
+def lazy_update(z: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor) -> Tensor:
+    """Block.lazy_workspace_update with gamma_from_alpha (local_thc.py:1278-1283, 1325-1328)."""
+    _require_cuda(z, dz, alpha, beta)
+    if z.shape != dz.shape or z.dim() < 1:
+        raise ValueError(f"lazy_update: z {tuple(z.shape)} and dz {tuple(dz.shape)} must match")
+    c = z.shape[-1]
+    _check_channels(c, "lazy_update")
+    _check_weight(alpha, c, "lazy_update")
+    _check_weight(beta, c, "lazy_update")
+    z, dz, alpha, beta = z.contiguous(), dz.to(z.dtype).contiguous(), alpha.contiguous(), beta.contiguous()
+    out = torch.empty_like(z)
+    n = z.numel() // c
+    with torch.cuda.device(z.device):
+        _lib.call("lthc_lazy_update_fwd", z.data_ptr(), dz.data_ptr(), alpha.data_ptr(), _code(alpha, "lazy_update"),
+                  beta.data_ptr(), _code(beta, "lazy_update"), out.data_ptr(), n, c, _code(z, "lazy_update"),
+                  _stream(z))
+    return out
+
+
+@lazy_update.register_fake
+def _(z, dz, alpha, beta):
+    return torch.empty_like(z)
+
+
+@torch.library.custom_op("lthc_b200::lazy_update_bwd", mutates_args=(), device_types="cuda")
+def lazy_update_bwd(grad_z_out: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """(grad_dz, grad_alpha fp32 [C,16], grad_beta fp32 [C,16]); grad_z is grad_z_out itself."""
+    _require_cuda(grad_z_out, dz, alpha, beta)
+    c = grad_z_out.shape[-1]
+    g, dz = grad_z_out.contiguous(), dz.to(grad_z_out.dtype).contiguous()
+    alpha, beta = alpha.contiguous(), beta.contiguous()
+    n = g.numel() // c
+    gdz = torch.empty_like(g)
+    ga = torch.empty((c, 16), device=g.device, dtype=torch.float32)
+    gb = torch.empty((c, 16), device=g.device, dtype=torch.float32)
+    with torch.cuda.device(g.device):
+        ws_bytes = _lib.load().lthc_lazy_update_bwd_workspace_bytes(n, c)
+        ws = _workspace(ws_bytes, g.device)
+        _lib.call("lthc_lazy_update_bwd", g.data_ptr(), dz.data_ptr(), alpha.data_ptr(),
+                  _code(alpha, "lazy_update_bwd"), beta.data_ptr(), _code(beta, "lazy_update_bwd"), gdz.data_ptr(),
+                  ga.data_ptr(), gb.data_ptr(), ws.data_ptr(), ws_bytes, n, c, _code(g, "lazy_update_bwd"), _stream(g))
+    return gdz, ga, gb
+
+
+@lazy_update_bwd.register_fake
+def _(grad_z_out, dz, alpha, beta):
+    c = grad_z_out.shape[-1]
+    return (torch.empty_like(grad_z_out), grad_z_out.new_empty((c, 16), dtype=torch.float32),
+            grad_z_out.new_empty((c, 16), dtype=torch.float32))
+
+
+def _lazy_setup(ctx, inputs, output):
+    z, dz, alpha, beta = inputs
+    ctx.save_for_backward(dz, alpha, beta)
+
+
+def _lazy_backward(ctx, grad_out):
+    dz, alpha, beta = ctx.saved_tensors
+    need_z, need_dz, need_a, need_b = ctx.needs_input_grad
+    gdz, ga, gb = lazy_update_bwd(grad_out, dz, alpha, beta)
+    return ((grad_out if need_z else None), (gdz.to(dz.dtype) if need_dz else None),
+            (ga.to(alpha.dtype) if need_a else None), (gb.to(beta.dtype) if need_b else None))
+
+
+lazy_update.register_autograd(_lazy_backward, setup_context=_lazy_setup)
+
+
+# ---------------------------------------------------------------------------
+# weight gradient  grad_w[l,c,r] = sum_cells high[cell,r,c] * low_l[cell,c]
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("lthc_b200::weight_grad", mutates_args=(), device_types="cuda")
+def weight_grad(high: Tensor, low: list[Tensor]) -> Tensor:
+    """[L,C,16] fp32, reduced in a fixed order (replaces the atomics of
+    _cell_weight_grad_kernel, local_thc_triton_kernels.py:167-199)."""
+    _require_cuda(high, *low)
+    b, g, c = _hi_geom(high, "weight_grad")
+    L = len(low)
+    if L < 1 or L > MAX_LAYERS:
+        raise ValueError(f"weight_grad: need 1..{MAX_LAYERS} workspace tensors, got {L}")
+    high = high.contiguous()
+    low = [t.to(high.dtype).contiguous() for t in low]
+    for t in low:
+        if tuple(t.shape) != (b, g * g, c):
+            raise ValueError(f"weight_grad: expected low [{b},{g * g},{c}], got {tuple(t.shape)}")
+    out = torch.empty((L, c, 16), device=high.device, dtype=torch.float32)
+    with torch.cuda.device(high.device):
+        ws_bytes = _lib.load().lthc_weight_grad_workspace_bytes(b, g, c, L)
+        ws = _workspace(ws_bytes, high.device)
+        _lib.call("lthc_weight_grad", high.data_ptr(), _lib.ptr_array([t.data_ptr() for t in low]), L, out.data_ptr(),
+                  ws.data_ptr(), ws_bytes, b, g, c, _code(high, "weight_grad"), _stream(high))
+    return out
+
+
+@weight_grad.register_fake
+def _(high, low):
+    return high.new_empty((len(low), high.shape[-1], 16), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# Mirrors of the reference jit_thc:: Triton op surface (same names and argument
+# order; "local_write" = read and "local_read" = write are that file's legacy
+# names, local_thc_triton_kernels.py:2673-2723).
+# ---------------------------------------------------------------------------
+def final_accumulate_b4_12_traceable(x0: Tensor, *dz_and_beta: Tensor) -> Tensor:
+    """jit_thc::final_accumulate_b4_12_traceable(x0, dz0..dz11, beta0..beta11) (:1669-1736)."""
+    if len(dz_and_beta) != 24:
+        raise ValueError(f"expected 12 dz and 12 beta tensors, got {len(dz_and_beta)} tensors")
+    return materialise(x0, list(dz_and_beta[:12]), list(dz_and_beta[12:]))
+
+
+def final_accumulate_b4_traceable(x0: Tensor, dz_stack: Tensor, beta_stack: Tensor) -> Tensor:
+    """jit_thc::final_accumulate_b4_traceable(x0, dz[L,B,256,C], beta[L,C,16]) (:1578-1598)."""
+    return materialise(x0, list(dz_stack.unbind(0)), list(beta_stack.unbind(0)))
+
+
+def final_accumulate_b4_12_grad_dz_ptr_traceable(grad_out: Tensor, *betas: Tensor) -> Tensor:
+    """jit_thc::final_accumulate_b4_12_grad_dz_ptr -> [12,B,256,C] (:1800-1845)."""
+    dummy = [grad_out.new_empty((grad_out.shape[0], (grad_out.shape[1] // 4) ** 2, grad_out.shape[3]))] * len(betas)
+    gdz, _ = materialise_bwd(grad_out, dummy, list(betas), True, False)
+    return torch.stack(gdz)
+
+
+def final_accumulate_b4_12_grad_beta_ptr_traceable(grad_out: Tensor, *dzs: Tensor) -> Tensor:
+    """jit_thc::final_accumulate_b4_12_grad_beta_ptr -> [12,C,16] fp32 (:1848-1894)."""
+    c = grad_out.shape[-1]
+    dummy = [grad_out.new_empty((c, 16), dtype=torch.float32)] * len(dzs)
+    _, gbeta = materialise_bwd(grad_out, list(dzs), dummy, False, True)
+    return gbeta
+
+
+def local_write_traceable(x: Tensor, weight: Tensor) -> Tensor:
+    """jit_thc::local_write_traceable = the read (:2673-2683)."""
+    return read(x, weight)
+
+
+def local_read_traceable(z: Tensor, weight: Tensor) -> Tensor:
+    """jit_thc::local_read_traceable = the write (:2686-2696)."""
+    return write(z, weight)
+
+
+def local_read_add_traceable(z: Tensor, weight: Tensor, x: Tensor) -> Tensor:
+    """jit_thc::local_read_add_traceable(z, weight, x) = x + write(z) (:2713-2723)."""
+    return write_add(x, z, weight)
+
+
+def local_weight_grad_traceable(high: Tensor, low: Tensor) -> Tensor:
+    """jit_thc::local_weight_grad_traceable(high, low) -> [C,16] fp32 (:2699-2710)."""
+    return weight_grad(high, [low])[0]
+
+
+__all__ = [
+    "read", "read_bwd", "write", "write_bwd", "write_add", "materialise", "materialise_bwd", "lazy_update",
+    "lazy_update_bwd", "weight_grad", "final_accumulate_b4_12_traceable", "final_accumulate_b4_traceable",
+    "final_accumulate_b4_12_grad_dz_ptr_traceable", "final_accumulate_b4_12_grad_beta_ptr_traceable",
+    "local_write_traceable", "local_read_traceable", "local_read_add_traceable", "local_weight_grad_traceable",
+]

@@ -1,0 +1,56 @@
+"""Shared pytest configuration.
+
+Tests marked ``gpu`` need a B200 (sm_100) and the built CUDA library; every
+other test runs on CPU.  ``-m "not gpu"`` is the CPU suite, ``-m gpu`` the
+parity suite.
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+REF = ROOT / "baseline" / "_ref"
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 GPU and the built liblthc_b200.so")
+    config.addinivalue_line("markers", "slow: full-size (benchmark-configuration) cases")
+
+
+def _cuda_ok() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available() and torch.cuda.get_device_capability(0)[0] == 10
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _cuda_ok():
+        return
+    skip = pytest.mark.skip(reason="no sm_100 GPU in this environment")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+def reference_available() -> bool:
+    """The reference package (tongtongliang/flowmatching_lthc) installed under baseline/_ref."""
+    return (REF / "flowmatching_lthc" / "__init__.py").exists()
+
+
+def import_reference():
+    if not reference_available():
+        pytest.skip("reference package not installed under baseline/_ref")
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
+    import flowmatching_lthc.models.local_thc as L  # noqa: F401
+    return L

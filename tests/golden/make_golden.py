@@ -1,0 +1,128 @@
+"""Generates the golden input/output fixtures under tests/golden/ by running the
+reference's own eager PyTorch code (tongtongliang/flowmatching_lthc) on CPU.
+
+Run from the repository root with the reference importable, e.g.
+
+    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py
+
+The reference is only needed to (re)generate the fixtures; the committed ``*.pt``
+files are what the tests read.  Every tensor is produced by the reference
+functions named below (paths inside the reference repository):
+
+  SharedLocalRead.read / .alpha          flowmatching_lthc/models/local_thc.py:1204-1223
+  LayerLocalWrite.write / .write_add     flowmatching_lthc/models/local_thc.py:1261-1276
+  LayerLocalWrite.gamma_from_alpha       flowmatching_lthc/models/local_thc.py:1278-1283
+  Block.lazy_workspace_update            flowmatching_lthc/models/local_thc.py:1325-1328
+  Model.final_accumulate_reference       flowmatching_lthc/models/local_thc.py:1368-1372
+
+Gradients come from torch.autograd through the same eager code.  Inputs follow
+the distributions of the benchmark configurations (X ~ N(0,1), read weights
+~ N(1/16, 0.01) used directly as alpha, write weights ~ N(0, 0.02), workspace
+updates ~ N(0,1) or N(0, 0.1)) at sizes small enough to commit.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, os.environ.get("LTHC_REFERENCE", "/root/reference"))
+sys.dont_write_bytecode = True
+
+from flowmatching_lthc.models import local_thc as L  # noqa: E402
+
+
+def cell_major_to_nhwc(x: torch.Tensor, g: int) -> torch.Tensor:
+    """[B, G*G, 16, C] cell-major -> NHWC [B, 4G, 4G, C] (cell (wy,wx), r = 4*row+col)."""
+    b, _, _, c = x.shape
+    return x.view(b, g, g, 4, 4, c).permute(0, 1, 3, 2, 4, 5).reshape(b, 4 * g, 4 * g, c).contiguous()
+
+
+def make_case(name: str, *, B: int, G: int, C: int, dtype: torch.dtype, depth: int, seed: int) -> dict:
+    gen = torch.Generator().manual_seed(seed)
+
+    def randn(*shape, mean=0.0, std=1.0):
+        return torch.randn(*shape, generator=gen) * std + mean
+
+    hi = 4 * G
+    x = cell_major_to_nhwc(randn(B, G * G, 16, C), G).to(dtype)
+    R = randn(C, 16, mean=1.0 / 16, std=0.01)
+    P = [randn(C, 16, std=0.02) for _ in range(depth)]
+    dz = [randn(B, G * G, C).to(dtype) for _ in range(depth)]
+    dz_small = [randn(B, G * G, C, std=0.1).to(dtype) for _ in range(depth)]
+    g_z = randn(B, G * G, C).to(dtype)
+    g_x = randn(B, hi, hi, C).to(dtype)
+
+    read = L.SharedLocalRead(hi, G, C, C, use_softmax_write=False)
+    read.read_logits.data.copy_(R)
+    writes = []
+    for l in range(depth):
+        w = L.LayerLocalWrite(hi, G, C, C)
+        w.write_weight.data.copy_(P[l])
+        writes.append(w)
+
+    out: dict = {"meta": {"name": name, "B": B, "G": G, "C": C, "dtype": str(dtype), "depth": depth, "seed": seed},
+                 "x": x, "R": R, "P": torch.stack(P), "dz": torch.stack(dz), "dz_small": torch.stack(dz_small),
+                 "g_z": g_z, "g_x": g_x}
+
+    # read (alpha = R directly, cast to the activation dtype as the module does)
+    xr = x.clone().requires_grad_(True)
+    z = read.read(xr)
+    gx, gR = torch.autograd.grad(z, (xr, read.read_logits), g_z)
+    out.update(read_z=z.detach(), read_gx=gx, read_gR=gR)
+
+    # write / write_add for layer 0
+    d0 = dz[0].clone().requires_grad_(True)
+    w0 = writes[0].write(d0)
+    gd, gP = torch.autograd.grad(w0, (d0, writes[0].write_weight), g_x)
+    out.update(write_out=w0.detach(), write_gdz=gd, write_gP=gP)
+    xa = x.clone().requires_grad_(True)
+    d0 = dz[0].clone().requires_grad_(True)
+    wa = writes[0].write_add(xa, d0)
+    gxa, gd, gP = torch.autograd.grad(wa, (xa, d0, writes[0].write_weight), g_x)
+    out.update(write_add_out=wa.detach(), write_add_gx=gxa, write_add_gdz=gd, write_add_gP=gP)
+
+    # gamma and the lazy workspace recurrence for layer 0
+    block = L.SharedReadLocalTHCSharedAdaLNJiTBlock(C, num_heads=C // 8, high_grid=hi, workspace_grid=G)
+    block.write.write_weight.data.copy_(P[0])
+    alpha = read.alpha(dtype=dtype)
+    out["gamma"] = block.write.gamma_from_alpha(alpha).detach()
+    zl = z.detach().clone().requires_grad_(True)
+    d0 = dz[0].clone().requires_grad_(True)
+    zn = block.lazy_workspace_update(zl, d0, read)
+    gzl, gd, gR, gP = torch.autograd.grad(zn, (zl, d0, read.read_logits, block.write.write_weight), g_z)
+    out.update(lazy_z=zn.detach(), lazy_gz=gzl, lazy_gdz=gd, lazy_gR=gR, lazy_gP=gP)
+
+    # materialisation over `depth` layers through the pure-torch accumulate loop
+    stub = types.SimpleNamespace(blocks=[types.SimpleNamespace(write=w) for w in writes])
+    x0 = x.clone().requires_grad_(True)
+    dzs = [t.clone().requires_grad_(True) for t in dz_small]
+    xl = L.SharedReadLocalTHCSharedAdaLNJiT.final_accumulate_reference(stub, x0, dzs)
+    grads = torch.autograd.grad(xl, (x0, *dzs, *[w.write_weight for w in writes]), g_x)
+    out.update(mat_out=xl.detach(), mat_gx0=grads[0], mat_gdz=torch.stack(grads[1:1 + depth]),
+               mat_gP=torch.stack(grads[1 + depth:]))
+    return out
+
+
+CASES = [
+    ("g4_c40_f32", dict(B=2, G=4, C=40, dtype=torch.float32, depth=12, seed=0)),
+    ("g4_c40_bf16", dict(B=2, G=4, C=40, dtype=torch.bfloat16, depth=12, seed=1)),
+    ("g16_c8_f32", dict(B=1, G=16, C=8, dtype=torch.float32, depth=12, seed=2)),
+    ("g2_c64_bf16", dict(B=3, G=2, C=64, dtype=torch.bfloat16, depth=3, seed=3)),
+]
+
+
+def main() -> None:
+    for name, kw in CASES:
+        case = make_case(name, **kw)
+        path = HERE / f"{name}.pt"
+        torch.save(case, path)
+        print(f"wrote {path} ({path.stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main()

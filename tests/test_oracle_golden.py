@@ -1,0 +1,145 @@
+"""Pins the C oracle against golden vectors produced by the reference's own eager
+PyTorch code (tests/golden/make_golden.py) and against the algebraic identities
+the reference documents.  CPU only."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import lthc_oracle as O
+
+CASES = ["g4_c40_f32", "g4_c40_bf16", "g16_c8_f32", "g2_c64_bf16"]
+# fp32: 1e-5 relative; bf16: 2e-2 (the reference's eager bf16 path rounds after
+# every product/sum, the oracle once)
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2}
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.double(), b.double()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+@pytest.fixture(scope="module", params=CASES)
+def case(request):
+    return torch.load(GOLDEN / f"{request.param}.pt")
+
+
+def test_read(case):
+    dt = case["x"].dtype
+    assert rel_err(O.read(case["x"], case["R"].to(dt)), case["read_z"]) < TOL[dt]
+
+
+def test_read_backward(case):
+    dt = case["x"].dtype
+    # grad_x = alpha (.) grad_z broadcast over the cell == write(grad_z, alpha)
+    assert rel_err(O.write(case["g_z"], case["R"].to(dt)), case["read_gx"]) < TOL[dt]
+    assert rel_err(O.weight_grad(case["x"], [case["g_z"]])[0], case["read_gR"]) < TOL[dt]
+
+
+def test_write_and_write_add(case):
+    dt = case["x"].dtype
+    P0 = case["P"][0].to(dt)
+    assert rel_err(O.write(case["dz"][0], P0), case["write_out"]) < TOL[dt]
+    assert rel_err(O.write_add(case["x"], case["dz"][0], P0), case["write_add_out"]) < TOL[dt]
+
+
+def test_write_backward(case):
+    dt = case["x"].dtype
+    gdz, gP = O.materialise_bwd(case["g_x"], [case["dz"][0]], [case["P"][0].to(dt)])
+    assert rel_err(gdz[0], case["write_gdz"]) < TOL[dt]
+    assert rel_err(gP[0], case["write_gP"]) < TOL[dt]
+    assert rel_err(gdz[0], case["write_add_gdz"]) < TOL[dt]
+    assert torch.equal(case["write_add_gx"], case["g_x"])  # identity branch of write_add
+
+
+def test_gamma_and_lazy(case):
+    dt = case["x"].dtype
+    a, p0 = case["R"].to(dt), case["P"][0].to(dt)
+    assert rel_err(O.lazy_fwd(case["read_z"], case["dz"][0], a, p0), case["lazy_z"]) < TOL[dt]
+    gdz, ga, gb = O.lazy_bwd(case["g_z"], case["dz"][0], a, p0)
+    assert rel_err(gdz, case["lazy_gdz"]) < TOL[dt]
+    assert rel_err(ga, case["lazy_gR"]) < TOL[dt]
+    assert rel_err(gb, case["lazy_gP"]) < TOL[dt]
+    assert torch.equal(case["lazy_gz"], case["g_z"])  # identity branch of the recurrence
+
+
+def test_materialise(case):
+    dt = case["x"].dtype
+    P = list(case["P"])
+    out = O.materialise(case["x"], list(case["dz_small"]), P)
+    assert rel_err(out, case["mat_out"]) < TOL[dt]
+
+
+def test_materialise_backward(case):
+    dt = case["x"].dtype
+    P = list(case["P"])
+    gdz, gP = O.materialise_bwd(case["g_x"], list(case["dz_small"]), P)
+    assert rel_err(torch.stack(gdz), case["mat_gdz"]) < TOL[dt]
+    assert rel_err(gP, case["mat_gP"]) < TOL[dt]
+    assert torch.equal(case["mat_gx0"], case["g_x"])  # grad X_0 is grad X_L
+
+
+def test_lazy_identity_read_of_write_is_gamma():
+    """R(P_l(dZ)) = Gamma_l (.) dZ (the identity behind the lazy recurrence,
+    docs/kernel_note.md:49-53 of the reference)."""
+    torch.manual_seed(0)
+    C, G = 24, 3
+    alpha = torch.softmax(torch.randn(C, 16), -1)
+    beta = torch.randn(C, 16) * 0.02 + 1.0
+    dz = torch.randn(2, G * G, C)
+    lhs = O.read(O.write(dz, beta), alpha)
+    gamma = (alpha * beta).sum(-1)
+    assert rel_err(lhs, gamma * dz) < 1e-6
+
+
+def test_lazy_equals_naive_recurrence():
+    """Z after L lazy updates equals the read of the materialised residual (fp64-exact
+    algebra, fp32 arithmetic): read(X_0 + sum_l P_l dZ_l) == read(X_0) + sum_l Gamma_l dZ_l."""
+    torch.manual_seed(1)
+    C, G, L = 16, 2, 5
+    alpha = torch.softmax(torch.randn(C, 16), -1)
+    betas = [torch.randn(C, 16) * 0.05 + 1.0 for _ in range(L)]
+    x0 = torch.randn(3, 4 * G, 4 * G, C)
+    dzs = [torch.randn(3, G * G, C) for _ in range(L)]
+    z = O.read(x0, alpha)
+    for d, b in zip(dzs, betas):
+        z = O.lazy_fwd(z, d, alpha, b)
+    naive = O.read(O.materialise(x0, dzs, betas), alpha)
+    assert rel_err(z, naive) < 1e-5
+
+
+def test_materialise_is_sequential_write_add_fp32():
+    torch.manual_seed(2)
+    C, G, L = 8, 2, 12
+    betas = [torch.randn(C, 16) for _ in range(L)]
+    x = torch.randn(2, 4 * G, 4 * G, C)
+    dzs = [torch.randn(2, G * G, C) for _ in range(L)]
+    seq = x
+    for d, b in zip(dzs, betas):
+        seq = O.write_add(seq, d, b)
+    assert rel_err(O.materialise(x, dzs, betas), seq) < 1e-6
+
+
+def test_empty_batch():
+    C, G = 8, 2
+    x = torch.empty(0, 4 * G, 4 * G, C)
+    assert O.read(x, torch.ones(C, 16)).shape == (0, G * G, C)
+    gw = O.weight_grad(x, [torch.empty(0, G * G, C)])
+    assert gw.shape == (1, C, 16) and torch.count_nonzero(gw) == 0
+
+
+def test_output_rounding_matches_torch_casts():
+    """The oracle rounds fp32 results to fp16/bf16 with IEEE round-to-nearest-even,
+    like torch's casts (values spanning subnormals to overflow)."""
+    from flowmatching_lthc_b200.workloads import cell_major_to_nhwc
+
+    torch.manual_seed(3)
+    C, G = 8, 8
+    scale = torch.logspace(-9, 5, G * G).view(1, G * G, 1)
+    for dt in (torch.float16, torch.bfloat16):
+        dz = (torch.randn(1, G * G, C) * scale).to(dt)
+        beta = torch.rand(C, 16) * 3
+        out = O.write(dz, beta)
+        ref = cell_major_to_nhwc(dz.float()[:, :, None, :] * beta.t()[None, None]).to(dt)
+        assert torch.equal(out.float(), ref.float())
