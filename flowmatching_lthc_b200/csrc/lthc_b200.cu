@@ -5,13 +5,20 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <type_traits>
+
+#include <cudaTypedefs.h>
 
 #include "lthc_b200.h"
 #include "lthc_common.cuh"
 #include "lthc_kernels.cuh"
+#include "lthc_tma.cuh"
+#include "lthc_broadcast_tma.cuh"
 
 namespace lthc {
+
 namespace {
 
 thread_local char g_last_error[512] = "";
@@ -23,9 +30,6 @@ int fail(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
-
-// Device-side error word (bounded waits that gave up, refused indices).
-__device__ int g_device_error = 0;
 
 struct DeviceInfo {
   int sms = 0;
@@ -93,6 +97,14 @@ int check_ptr(const void* p, const char* name) {
   return LTHC_OK;
 }
 
+// Activation tensors may be NULL when they are empty (torch gives empty tensors a
+// null data pointer); everything else is checked like check_ptr.
+int check_act(const void* p, const char* name, bool nonempty) {
+  if (!p) return nonempty ? fail(LTHC_ERR_NULL_POINTER, "%s is NULL", name) : LTHC_OK;
+  if (!aligned16(p)) return fail(LTHC_ERR_ALIGNMENT, "%s is not 16-byte aligned", name);
+  return LTHC_OK;
+}
+
 int check_layers(int L) {
   if (L < 1 || L > kMaxLayers) return fail(LTHC_ERR_SHAPE, "n_layers must be in [1, %d], got %d", kMaxLayers, L);
   return LTHC_OK;
@@ -147,32 +159,135 @@ size_t lazy_ws_bytes(int64_t N, int64_t C, int sms) {
   return static_cast<size_t>(plan_grid_stride(N, C, sms, 4, kLazyWarps)) * C * sizeof(float);
 }
 
-// ---- dispatch helpers -----------------------------------------------------
-template <typename T>
-int launch_broadcast(BroadcastParams p, int L, bool has_base, int sms, cudaStream_t s) {
-  const CellPlan pl = plan_cells(p.cells, p.C, sms, 8, 4);
-  p.cells_per_block = pl.cells_per_block;
-  dim3 grid(static_cast<unsigned>(pl.blocks_x), static_cast<unsigned>(slices_of(p.C)));
-  if (L == 1) {
-    if (has_base) broadcast_kernel<T, 1, true><<<grid, 128, 0, s>>>(p);
-    else broadcast_kernel<T, 1, false><<<grid, 128, 0, s>>>(p);
-  } else if (L == 12) {
-    if (has_base) broadcast_kernel<T, 12, true><<<grid, 128, 0, s>>>(p);
-    else broadcast_kernel<T, 12, false><<<grid, 128, 0, s>>>(p);
-  } else {
-    if (has_base) broadcast_kernel<T, 0, true><<<grid, 128, 0, s>>>(p);
-    else broadcast_kernel<T, 0, false><<<grid, 128, 0, s>>>(p);
-  }
-  return launched("broadcast");
+// ---- TMA tensor maps ---------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q{};
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cudaGetLastError();
+  });
+  return fn;
 }
 
-int broadcast(BroadcastParams p, int L, bool has_base, int act, cudaStream_t s) {
+template <typename T>
+CUtensorMapDataType tmap_dtype() {
+  if constexpr (sizeof(T) == 4) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  else if constexpr (std::is_same_v<T, __nv_bfloat16>) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  else return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// NHWC residual [B, 4G, 4G, C] as a 4-D map (C, W, H, B); box = 64 channels x 16
+// columns x 4 rows x 1 image (one strip of 4 cells).
+template <typename T>
+int encode_residual_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t G, int64_t C) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(LTHC_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t es = sizeof(T);
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(4 * G),
+                              static_cast<cuuint64_t>(4 * G), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {C * es, 4 * G * C * es, 16 * G * G * C * es};
+  const cuuint32_t box[4] = {kSliceCh, 16, 4, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, tmap_dtype<T>(), 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (residual) failed with %d", (int)r);
+  return LTHC_OK;
+}
+
+// Workspace [rows, C] as a 2-D map; box = 64 channels x 4 rows (one strip).
+template <typename T>
+int encode_workspace_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t C) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(LTHC_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t es = sizeof(T);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {C * es};
+  const cuuint32_t box[2] = {kSliceCh, kStripCells};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, tmap_dtype<T>(), 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (workspace) failed with %d", (int)r);
+  return LTHC_OK;
+}
+
+// Per-device, per-kernel one-time set-up: opt in to the dynamic shared memory the
+// kernel needs and record how many CTAs fit on one SM.
+template <typename Kernel>
+int resident_ctas(Kernel kern, int threads, int smem_bytes, int* out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return launched("cudaGetDevice");
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+      return launched("cudaFuncSetAttribute");
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem_bytes) != cudaSuccess)
+      return launched("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    it = cache.emplace(key, std::max(n, 1)).first;
+  }
+  *out = it->second;
+  return LTHC_OK;
+}
+
+// ---- dispatch helpers -----------------------------------------------------
+template <typename T, int LT, bool HB>
+int launch_broadcast_tma(BcastTmaParams& p, int sms, cudaStream_t s) {
+  using Lay = BcastLayout<T, (LT > 0 ? LT : kMaxLayers)>;
+  auto kern = broadcast_tma_kernel<T, LT, HB>;
+  int per_sm = 1;
+  LTHC_TRY(resident_ctas(kern, kBcastThreads, Lay::kSmemBytes, &per_sm));
+  const int64_t slices = slices_of(p.C);
+  int64_t nx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
+  nx = std::max<int64_t>(1, std::min<int64_t>(nx, p.strips));
+  p.strips_per_cta = ceil_div(p.strips, nx);
+  nx = ceil_div(p.strips, p.strips_per_cta);
+  kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), kBcastThreads, Lay::kSmemBytes, s>>>(p);
+  return launched("broadcast (TMA)");
+}
+
+template <typename T>
+int broadcast_t(const void* base, const void* const* dz, const void* const* w, int w_dtype, int L, void* out,
+                int64_t B, int64_t G, int64_t C, int sms, cudaStream_t s) {
+  BcastTmaParams p;
+  memset(&p, 0, sizeof(p));
+  if (base) LTHC_TRY(encode_residual_map<T>(&p.tm_base, base, B, G, C));
+  for (int l = 0; l < L; ++l) {
+    LTHC_TRY(encode_workspace_map<T>(&p.tm_dz[l], dz[l], B * G * G, C));
+    p.w[l] = w[l];
+  }
+  p.out = out;
+  p.w_dtype = w_dtype;
+  p.L = L;
+  p.G = static_cast<int>(G);
+  p.strips_per_row = static_cast<int>(ceil_div(G, kStripCells));
+  p.C = C;
+  p.strips = B * G * p.strips_per_row;
+  const bool hb = base != nullptr;
+  if (L == 12) return hb ? launch_broadcast_tma<T, 12, true>(p, sms, s) : launch_broadcast_tma<T, 12, false>(p, sms, s);
+  if (L == 1) return hb ? launch_broadcast_tma<T, 1, true>(p, sms, s) : launch_broadcast_tma<T, 1, false>(p, sms, s);
+  return hb ? launch_broadcast_tma<T, 0, true>(p, sms, s) : launch_broadcast_tma<T, 0, false>(p, sms, s);
+}
+
+// out = base + sum_{l<L} w_l (.) dz_l  (base may be NULL)
+int broadcast(const void* base, const void* const* dz, const void* const* w, int w_dtype, int L, void* out, int64_t B,
+              int64_t G, int64_t C, int act, cudaStream_t s) {
   int sms = 0;
   LTHC_TRY(current_device(&sms));
   switch (act) {
-    case LTHC_DTYPE_F32: return launch_broadcast<float>(p, L, has_base, sms, s);
-    case LTHC_DTYPE_BF16: return launch_broadcast<__nv_bfloat16>(p, L, has_base, sms, s);
-    default: return launch_broadcast<__half>(p, L, has_base, sms, s);
+    case LTHC_DTYPE_F32: return broadcast_t<float>(base, dz, w, w_dtype, L, out, B, G, C, sms, s);
+    case LTHC_DTYPE_BF16: return broadcast_t<__nv_bfloat16>(base, dz, w, w_dtype, L, out, B, G, C, sms, s);
+    default: return broadcast_t<__half>(base, dz, w, w_dtype, L, out, B, G, C, sms, s);
   }
 }
 
@@ -329,43 +444,27 @@ int lthc_write_fwd(const void* dz, const void* beta, int beta_dtype, void* out, 
                    int act_dtype, void* stream) {
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
-  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_act(dz, "dz", B > 0));
   LTHC_TRY(check_ptr(beta, "beta"));
-  LTHC_TRY(check_ptr(out, "out"));
+  LTHC_TRY(check_act(out, "out", B > 0));
   if (B == 0) return LTHC_OK;
-  BroadcastParams p{};
-  p.base = nullptr;
-  p.dz[0] = dz;
-  p.w[0] = beta;
-  p.out = out;
-  p.w_dtype = beta_dtype;
-  p.L = 1;
-  p.G = static_cast<int>(G);
-  p.C = C;
-  p.cells = B * G * G;
-  return broadcast(p, 1, false, act_dtype, static_cast<cudaStream_t>(stream));
+  const void* dzs[1] = {dz};
+  const void* ws[1] = {beta};
+  return broadcast(nullptr, dzs, ws, beta_dtype, 1, out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int lthc_write_add_fwd(const void* x, const void* dz, const void* beta, int beta_dtype, void* out, int64_t B,
                        int64_t G, int64_t C, int act_dtype, void* stream) {
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
-  LTHC_TRY(check_ptr(x, "x"));
-  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_act(x, "x", B > 0));
+  LTHC_TRY(check_act(dz, "dz", B > 0));
   LTHC_TRY(check_ptr(beta, "beta"));
-  LTHC_TRY(check_ptr(out, "out"));
+  LTHC_TRY(check_act(out, "out", B > 0));
   if (B == 0) return LTHC_OK;
-  BroadcastParams p{};
-  p.base = x;
-  p.dz[0] = dz;
-  p.w[0] = beta;
-  p.out = out;
-  p.w_dtype = beta_dtype;
-  p.L = 1;
-  p.G = static_cast<int>(G);
-  p.C = C;
-  p.cells = B * G * G;
-  return broadcast(p, 1, true, act_dtype, static_cast<cudaStream_t>(stream));
+  const void* dzs[1] = {dz};
+  const void* ws[1] = {beta};
+  return broadcast(x, dzs, ws, beta_dtype, 1, out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int lthc_materialise_fwd(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype,
@@ -374,26 +473,14 @@ int lthc_materialise_fwd(const void* x0, const void* const* dz, const void* cons
   LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
   LTHC_TRY(check_layers(n_layers));
   if (!dz || !beta) return fail(LTHC_ERR_NULL_POINTER, "dz / beta pointer arrays are NULL");
-  if (x0) LTHC_TRY(check_ptr(x0, "x0"));
-  LTHC_TRY(check_ptr(out, "out"));
+  if (x0) LTHC_TRY(check_act(x0, "x0", B > 0));
+  LTHC_TRY(check_act(out, "out", B > 0));
   for (int l = 0; l < n_layers; ++l) {
-    LTHC_TRY(check_ptr(dz[l], "dz[l]"));
+    LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
     LTHC_TRY(check_ptr(beta[l], "beta[l]"));
   }
   if (B == 0) return LTHC_OK;
-  BroadcastParams p{};
-  p.base = x0;
-  for (int l = 0; l < n_layers; ++l) {
-    p.dz[l] = dz[l];
-    p.w[l] = beta[l];
-  }
-  p.out = out;
-  p.w_dtype = beta_dtype;
-  p.L = n_layers;
-  p.G = static_cast<int>(G);
-  p.C = C;
-  p.cells = B * G * G;
-  return broadcast(p, n_layers, x0 != nullptr, act_dtype, static_cast<cudaStream_t>(stream));
+  return broadcast(x0, dz, beta, beta_dtype, n_layers, out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int lthc_materialise12_fwd(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype,
@@ -412,19 +499,19 @@ int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
   LTHC_TRY(check_layers(n_layers));
-  LTHC_TRY(check_ptr(grad_out, "grad_out"));
+  LTHC_TRY(check_act(grad_out, "grad_out", B > 0));
   if (!grad_dz && !grad_beta) return LTHC_OK;
   if (grad_dz) {
     if (!beta) return fail(LTHC_ERR_NULL_POINTER, "beta pointer array is NULL");
     for (int l = 0; l < n_layers; ++l) {
       LTHC_TRY(check_ptr(beta[l], "beta[l]"));
-      LTHC_TRY(check_ptr(grad_dz[l], "grad_dz[l]"));
+      LTHC_TRY(check_act(grad_dz[l], "grad_dz[l]", B > 0));
     }
   }
   if (grad_beta) {
     if (!dz) return fail(LTHC_ERR_NULL_POINTER, "dz pointer array is NULL");
     LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
-    for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_ptr(dz[l], "dz[l]"));
+    for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (grad_beta) {
@@ -461,9 +548,9 @@ int lthc_read_fwd(const void* x, const void* alpha, int alpha_dtype, void* z, in
                   int act_dtype, void* stream) {
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_weight_dtype(alpha_dtype, "alpha"));
-  LTHC_TRY(check_ptr(x, "x"));
+  LTHC_TRY(check_act(x, "x", B > 0));
   LTHC_TRY(check_ptr(alpha, "alpha"));
-  LTHC_TRY(check_ptr(z, "z"));
+  LTHC_TRY(check_act(z, "z", B > 0));
   if (B == 0) return LTHC_OK;
   const void* w[1] = {alpha};
   void* out[1] = {z};
@@ -478,10 +565,10 @@ int lthc_weight_grad(const void* high, const void* const* low, int n_layers, flo
                      size_t workspace_bytes, int64_t B, int64_t G, int64_t C, int act_dtype, void* stream) {
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_layers(n_layers));
-  LTHC_TRY(check_ptr(high, "high"));
+  LTHC_TRY(check_act(high, "high", B > 0));
   LTHC_TRY(check_ptr(grad_w, "grad_w"));
   if (!low) return fail(LTHC_ERR_NULL_POINTER, "low pointer array is NULL");
-  for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_ptr(low[l], "low[l]"));
+  for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(low[l], "low[l]", B > 0));
   return weight_grad_impl(high, low, n_layers, grad_w, workspace, workspace_bytes, B, G, C, act_dtype,
                           static_cast<cudaStream_t>(stream));
 }
@@ -495,10 +582,10 @@ int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alph
                   int64_t C, int act_dtype, void* stream) {
   LTHC_TRY(check_geometry(B, G, C, act_dtype));
   LTHC_TRY(check_weight_dtype(alpha_dtype, "alpha"));
-  LTHC_TRY(check_ptr(grad_z, "grad_z"));
+  LTHC_TRY(check_act(grad_z, "grad_z", B > 0));
   LTHC_TRY(check_ptr(alpha, "alpha"));
-  if (grad_x_in) LTHC_TRY(check_ptr(grad_x_in, "grad_x_in"));
-  if (grad_alpha) LTHC_TRY(check_ptr(x, "x"));
+  if (grad_x_in) LTHC_TRY(check_act(grad_x_in, "grad_x_in", B > 0));
+  if (grad_alpha) LTHC_TRY(check_act(x, "x", B > 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (grad_alpha) {
     int sms = 0;
@@ -509,19 +596,11 @@ int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alph
                   need);
   }
   if (grad_x) {
-    LTHC_TRY(check_ptr(grad_x, "grad_x"));
+    LTHC_TRY(check_act(grad_x, "grad_x", B > 0));
     if (B > 0) {
-      BroadcastParams p{};
-      p.base = grad_x_in;
-      p.dz[0] = grad_z;
-      p.w[0] = alpha;
-      p.out = grad_x;
-      p.w_dtype = alpha_dtype;
-      p.L = 1;
-      p.G = static_cast<int>(G);
-      p.C = C;
-      p.cells = B * G * G;
-      LTHC_TRY(broadcast(p, 1, grad_x_in != nullptr, act_dtype, s));
+      const void* dzs[1] = {grad_z};
+      const void* ws[1] = {alpha};
+      LTHC_TRY(broadcast(grad_x_in, dzs, ws, alpha_dtype, 1, grad_x, B, G, C, act_dtype, s));
     }
   }
   if (grad_alpha) {
@@ -546,11 +625,11 @@ static int check_lazy(int64_t N, int64_t C, int act_dtype, int a_dtype, int b_dt
 int lthc_lazy_update_fwd(const void* z, const void* dz, const void* alpha, int alpha_dtype, const void* beta,
                          int beta_dtype, void* z_out, int64_t N, int64_t C, int act_dtype, void* stream) {
   LTHC_TRY(check_lazy(N, C, act_dtype, alpha_dtype, beta_dtype));
-  LTHC_TRY(check_ptr(z, "z"));
-  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_act(z, "z", N > 0));
+  LTHC_TRY(check_act(dz, "dz", N > 0));
   LTHC_TRY(check_ptr(alpha, "alpha"));
   LTHC_TRY(check_ptr(beta, "beta"));
-  LTHC_TRY(check_ptr(z_out, "z_out"));
+  LTHC_TRY(check_act(z_out, "z_out", N > 0));
   if (N == 0) return LTHC_OK;
   int sms = 0;
   LTHC_TRY(current_device(&sms));
@@ -575,11 +654,11 @@ int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alp
                          void* workspace, size_t workspace_bytes, int64_t N, int64_t C, int act_dtype,
                          void* stream) {
   LTHC_TRY(check_lazy(N, C, act_dtype, alpha_dtype, beta_dtype));
-  LTHC_TRY(check_ptr(grad_z_out, "grad_z_out"));
-  LTHC_TRY(check_ptr(dz, "dz"));
+  LTHC_TRY(check_act(grad_z_out, "grad_z_out", N > 0));
+  LTHC_TRY(check_act(dz, "dz", N > 0));
   LTHC_TRY(check_ptr(alpha, "alpha"));
   LTHC_TRY(check_ptr(beta, "beta"));
-  LTHC_TRY(check_ptr(grad_dz, "grad_dz"));
+  LTHC_TRY(check_act(grad_dz, "grad_dz", N > 0));
   if (grad_alpha) LTHC_TRY(check_ptr(grad_alpha, "grad_alpha"));
   if (grad_beta) LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
   int sms = 0;

@@ -12,84 +12,6 @@
 namespace lthc {
 
 // ---------------------------------------------------------------------------
-// write family: out[cell, r, c] = base[cell, r, c] + sum_l w_l[c, r] * dz_l[cell, c]
-// (write: no base, L=1; write_add: base, L=1; materialise: base, L=12;
-//  read backward: gx = (gx_in +) alpha (.) gz, L=1.)
-// Thread (lane, warp) = (channel pair, cell row); it keeps w_l[c, 4*row + col]
-// for its 4 columns in registers (8*L floats) and per cell issues 4 base loads,
-// L workspace loads (shared by the 4 row-warps through L1) and 4 stores.
-// The accumulation order is base, then l = 0, 1, ... (the Triton op's order,
-// local_thc_triton_kernels.py:363-403).
-// ---------------------------------------------------------------------------
-struct BroadcastParams {
-  const void* base;                 // T[B,4G,4G,C] or nullptr
-  const void* dz[kMaxLayers];       // T[B,G*G,C]
-  const void* w[kMaxLayers];        // [C,16], dtype w_dtype
-  void* out;                        // T[B,4G,4G,C]
-  int w_dtype;
-  int L;
-  int G;
-  int64_t C;
-  int64_t cells;                    // B*G*G
-  int64_t cells_per_block;
-};
-
-template <typename T, int LT, bool HAS_BASE>
-__global__ void __launch_bounds__(128) broadcast_kernel(const __grid_constant__ BroadcastParams p) {
-  constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
-  const int L = LT > 0 ? LT : p.L;
-  const int lane = threadIdx.x & 31;
-  const int row = threadIdx.x >> 5;
-  const int64_t c = static_cast<int64_t>(blockIdx.y) * kSliceCh + 2 * lane;
-  if (c >= p.C) return;
-
-  float2 w[LMAX][4];
-#pragma unroll
-  for (int l = 0; l < LMAX; ++l) {
-#pragma unroll
-    for (int col = 0; col < 4; ++col) {
-      if (l < L) {
-        w[l][col].x = load_weight(p.w[l], p.w_dtype, c * kPos + row * 4 + col);
-        w[l][col].y = load_weight(p.w[l], p.w_dtype, (c + 1) * kPos + row * 4 + col);
-      } else {
-        w[l][col] = make_float2(0.f, 0.f);
-      }
-    }
-  }
-
-  const T* base = static_cast<const T*>(p.base);
-  T* out = static_cast<T*>(p.out);
-  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * p.cells_per_block;
-  const int64_t m1 = min(m0 + p.cells_per_block, p.cells);
-#pragma unroll 2
-  for (int64_t m = m0; m < m1; ++m) {
-    const int64_t tok = cell_token_offset(m, p.G, p.C, row, 0) + c;
-    float2 acc[4];
-    if constexpr (HAS_BASE) {
-      typename Act<T>::Raw raw[4];
-#pragma unroll
-      for (int col = 0; col < 4; ++col) raw[col] = Act<T>::ld_stream(base + tok + col * p.C);
-#pragma unroll
-      for (int col = 0; col < 4; ++col) acc[col] = Act<T>::cvt(raw[col]);
-    } else {
-#pragma unroll
-      for (int col = 0; col < 4; ++col) acc[col] = make_float2(0.f, 0.f);
-    }
-    const int64_t zoff = m * p.C + c;
-#pragma unroll
-    for (int l = 0; l < LMAX; ++l) {
-      if (l < L) {
-        const float2 d = Act<T>::cvt(Act<T>::ld(static_cast<const T*>(p.dz[l]) + zoff));
-#pragma unroll
-        for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
-      }
-    }
-#pragma unroll
-    for (int col = 0; col < 4; ++col) Act<T>::st_stream(out + tok + col * p.C, acc[col]);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // read (single weight set): z[cell, c] = sum_r w[c, r] * x[cell, r, c]
 // Thread (lane, warp) = (channel pair, cell stream); 16 weights per channel in
 // registers, 16 independent loads per cell, sum in position order r = 0..15.
