@@ -16,6 +16,7 @@
 #include "lthc_kernels.cuh"
 #include "lthc_tma.cuh"
 #include "lthc_broadcast_tma.cuh"
+#include "lthc_pool_tma.cuh"
 
 namespace lthc {
 
@@ -126,32 +127,29 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 int64_t slices_of(int64_t C) { return ceil_div(C, kSliceCh); }
 
 // ---- grid plans (pure functions of the problem size and the SM count) ------
-struct CellPlan {
-  int64_t blocks_x;
-  int64_t cells_per_block;
-};
-
-// CTAs that each walk a contiguous range of cells; about `per_sm` CTAs per SM.
-CellPlan plan_cells(int64_t cells, int64_t C, int sms, int per_sm, int64_t min_cells) {
-  const int64_t slices = slices_of(C);
-  int64_t bx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
-  bx = std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(cells, min_cells)));
-  const int64_t cpb = ceil_div(cells, bx);
-  return CellPlan{ceil_div(cells, cpb), cpb};
-}
-
-CellPlan plan_wgrad(int64_t cells, int64_t C, int sms) { return plan_cells(cells, C, sms, 4, 16); }
-
 int64_t plan_grid_stride(int64_t rows, int64_t C, int sms, int per_sm, int rows_per_block) {
   const int64_t slices = slices_of(C);
   int64_t bx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
   return std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(rows, rows_per_block)));
 }
 
-size_t wgrad_ws_bytes(int64_t cells, int64_t C, int L, int sms) {
-  if (cells <= 0) return 0;
-  const CellPlan pl = plan_wgrad(cells, C, sms);
-  return static_cast<size_t>(pl.blocks_x) * L * C * kPos * sizeof(float);
+// Weight-gradient partials: one [L][C][16] fp32 block per CTA column of the read
+// kernel, whose grid is fixed at two CTAs per SM so that the workspace size is a
+// pure function of the shape and the SM count.
+constexpr int kWgradCtasPerSm = 2;
+
+int64_t strips_of(int64_t B, int64_t G) { return B * G * ceil_div(G, kStripCells); }
+
+int64_t wgrad_blocks(int64_t strips, int64_t C, int sms) {
+  const int64_t nx = std::max<int64_t>(1, std::min<int64_t>(ceil_div(static_cast<int64_t>(sms) * kWgradCtasPerSm,
+                                                                     slices_of(C)),
+                                                            strips));
+  return ceil_div(strips, ceil_div(strips, nx));
+}
+
+size_t wgrad_ws_bytes(int64_t B, int64_t G, int64_t C, int L, int sms) {
+  if (B <= 0) return 0;
+  return static_cast<size_t>(wgrad_blocks(strips_of(B, G), C, sms)) * L * C * kPos * sizeof(float);
 }
 
 size_t lazy_ws_bytes(int64_t N, int64_t C, int sms) {
@@ -291,104 +289,97 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
   }
 }
 
+// ---- read family -------------------------------------------------------------
+struct ReadJob {
+  const void* h;               // residual-sized input
+  const void* const* w;        // POOL weights
+  int w_dtype;
+  void* const* out;            // POOL outputs (nullptr: no pooling)
+  const void* const* low;      // WGRAD workspace-sized inputs
+  float* grad_w;               // WGRAD result [L][C][16] (nullptr: no weight gradient)
+  void* ws;                    // WGRAD partials
+  int L;
+  int64_t B, G, C;
+};
+
+template <typename T, int LT, bool POOL, bool WGRAD, int CPP>
+int launch_read_t(PoolTmaParams& p, float* grad_w, int sms, cudaStream_t s) {
+  using Lay = PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL, WGRAD, CPP>;
+  auto kern = pool_tma_kernel<T, LT, POOL, WGRAD, CPP>;
+  int per_sm = 1;
+  LTHC_TRY(resident_ctas(kern, Lay::kThreads, Lay::kSmemBytes, &per_sm));
+  const int64_t slices = slices_of(p.C);
+  int64_t nx = WGRAD ? wgrad_blocks(p.strips, p.C, sms)
+                     : std::max<int64_t>(1, std::min<int64_t>(ceil_div(static_cast<int64_t>(sms) * per_sm, slices),
+                                                              p.strips));
+  p.strips_per_cta = ceil_div(p.strips, nx);
+  nx = ceil_div(p.strips, p.strips_per_cta);
+  kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), Lay::kThreads, Lay::kSmemBytes, s>>>(p);
+  LTHC_TRY(launched("read family (TMA)"));
+  if (WGRAD) {
+    const int64_t n = static_cast<int64_t>(p.L) * p.C * kPos;
+    const int64_t rb = std::min<int64_t>(ceil_div(n, 256), static_cast<int64_t>(sms) * 8);
+    reduce_partials_kernel<<<static_cast<unsigned>(rb), 256, 0, s>>>(p.partial, grad_w, n, static_cast<int>(nx));
+    LTHC_TRY(launched("weight-grad reduce"));
+  }
+  return LTHC_OK;
+}
+
+template <typename T, bool POOL, bool WGRAD>
+int launch_read_l(PoolTmaParams& p, float* grad_w, int sms, cudaStream_t s) {
+  if (p.L == 1) return launch_read_t<T, 1, POOL, WGRAD, 1>(p, grad_w, sms, s);
+  if (p.L == 12) return launch_read_t<T, 12, POOL, WGRAD, 4>(p, grad_w, sms, s);
+  return launch_read_t<T, 0, POOL, WGRAD, 4>(p, grad_w, sms, s);
+}
+
 template <typename T>
-int launch_pool1(const PoolParams& p, int sms, cudaStream_t s) {
-  const int64_t bx = plan_grid_stride(p.cells, p.C, sms, 8, kPoolWarps);
-  dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(slices_of(p.C)));
-  pool1_kernel<T><<<grid, 32 * kPoolWarps, 0, s>>>(p);
-  return launched("read");
+int read_family_t(const ReadJob& j, int sms, cudaStream_t s) {
+  PoolTmaParams p;
+  memset(&p, 0, sizeof(p));
+  const bool pool = j.out != nullptr;
+  const bool wgrad = j.grad_w != nullptr;
+  LTHC_TRY(encode_residual_map<T>(&p.tm_h, j.h, j.B, j.G, j.C));
+  for (int l = 0; l < j.L; ++l) {
+    if (pool) {
+      p.w[l] = j.w[l];
+      p.out[l] = j.out[l];
+    }
+    if (wgrad) LTHC_TRY(encode_workspace_map<T>(&p.tm_low[l], j.low[l], j.B * j.G * j.G, j.C));
+  }
+  p.partial = wgrad ? static_cast<float*>(j.ws) : nullptr;
+  p.w_dtype = j.w_dtype;
+  p.L = j.L;
+  p.G = static_cast<int>(j.G);
+  p.strips_per_row = static_cast<int>(ceil_div(j.G, kStripCells));
+  p.C = j.C;
+  p.strips = strips_of(j.B, j.G);
+  if (pool && wgrad) return launch_read_l<T, true, true>(p, j.grad_w, sms, s);
+  if (pool) return launch_read_l<T, true, false>(p, nullptr, sms, s);
+  return launch_read_l<T, false, true>(p, j.grad_w, sms, s);
 }
 
-template <typename T, int LT>
-int launch_pool_multi_t(const PoolMultiParams& p, int sms, cudaStream_t s) {
-  constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
-  const size_t smem = sizeof(float2) * kPos * LMAX * 32;
-  static_assert(sizeof(float2) * kPos * LMAX * 32 <= 48 * 1024, "weight slice must fit the default 48 KB");
-  const int64_t bx = plan_grid_stride(p.cells, p.C, sms, 4, kPoolWarps);
-  dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(slices_of(p.C)));
-  pool_multi_kernel<T, LT><<<grid, 32 * kPoolWarps, smem, s>>>(p);
-  return launched("read (multi-layer)");
-}
-
-template <typename T>
-int launch_pool_multi(const PoolMultiParams& p, int sms, cudaStream_t s) {
-  if (p.L == 12) return launch_pool_multi_t<T, 12>(p, sms, s);
-  if (p.L == 1) return launch_pool_multi_t<T, 1>(p, sms, s);
-  return launch_pool_multi_t<T, 0>(p, sms, s);
-}
-
-template <typename T>
-int launch_wgrad(WgradParams p, float* out, int sms, cudaStream_t s) {
-  const CellPlan pl = plan_wgrad(p.cells, p.C, sms);
-  p.cells_per_block = pl.cells_per_block;
-  dim3 grid(static_cast<unsigned>(pl.blocks_x), static_cast<unsigned>(slices_of(p.C)));
-  if (p.L == 12) wgrad_kernel<T, 12><<<grid, 128, 0, s>>>(p);
-  else if (p.L == 1) wgrad_kernel<T, 1><<<grid, 128, 0, s>>>(p);
-  else wgrad_kernel<T, 0><<<grid, 128, 0, s>>>(p);
-  LTHC_TRY(launched("weight-grad"));
-  const int64_t n = static_cast<int64_t>(p.L) * p.C * kPos;
-  const int64_t rb = std::min<int64_t>(ceil_div(n, 256), static_cast<int64_t>(sms) * 8);
-  reduce_partials_kernel<<<static_cast<unsigned>(rb), 256, 0, s>>>(p.partial, out, n, static_cast<int>(pl.blocks_x));
-  return launched("weight-grad reduce");
-}
-
-int weight_grad_impl(const void* high, const void* const* low, int L, float* grad_w, void* ws, size_t ws_bytes,
-                     int64_t B, int64_t G, int64_t C, int act, cudaStream_t s) {
+// Runs the read-family kernel (pooling and/or weight gradient).  The caller has
+// validated pointers; this checks the workspace and handles the empty batch.
+int read_family(const ReadJob& j, size_t ws_bytes, int act, cudaStream_t s) {
+  if (!j.out && !j.grad_w) return LTHC_OK;
   int sms = 0;
   LTHC_TRY(current_device(&sms));
-  const int64_t cells = B * G * G;
-  if (cells == 0) {
-    // Empty batch: the gradient is exactly zero.
-    if (cudaMemsetAsync(grad_w, 0, sizeof(float) * L * C * kPos, s) != cudaSuccess) return launched("memset");
+  if (j.B == 0) {
+    // Empty batch: pooled outputs are empty, the weight gradient is exactly zero.
+    if (j.grad_w && cudaMemsetAsync(j.grad_w, 0, sizeof(float) * j.L * j.C * kPos, s) != cudaSuccess)
+      return launched("memset");
     return LTHC_OK;
   }
-  const size_t need = wgrad_ws_bytes(cells, C, L, sms);
-  if (!ws || ws_bytes < need)
-    return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
-  if (!aligned16(ws)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
-  WgradParams p{};
-  p.high = high;
-  for (int l = 0; l < L; ++l) p.low[l] = low[l];
-  p.partial = static_cast<float*>(ws);
-  p.L = L;
-  p.G = static_cast<int>(G);
-  p.C = C;
-  p.cells = cells;
-  switch (act) {
-    case LTHC_DTYPE_F32: return launch_wgrad<float>(p, grad_w, sms, s);
-    case LTHC_DTYPE_BF16: return launch_wgrad<__nv_bfloat16>(p, grad_w, sms, s);
-    default: return launch_wgrad<__half>(p, grad_w, sms, s);
-  }
-}
-
-int pool_multi_impl(const void* x, const void* const* w, int w_dtype, int L, void* const* out, int64_t B,
-                    int64_t G, int64_t C, int act, cudaStream_t s) {
-  int sms = 0;
-  LTHC_TRY(current_device(&sms));
-  PoolMultiParams p{};
-  p.x = x;
-  for (int l = 0; l < L; ++l) {
-    p.w[l] = w[l];
-    p.out[l] = out[l];
-  }
-  p.w_dtype = w_dtype;
-  p.L = L;
-  p.G = static_cast<int>(G);
-  p.C = C;
-  p.cells = B * G * G;
-  if (p.cells == 0) return LTHC_OK;
-  if (L == 1) {
-    PoolParams q{x, w[0], out[0], w_dtype, static_cast<int>(G), C, p.cells};
-    switch (act) {
-      case LTHC_DTYPE_F32: return launch_pool1<float>(q, sms, s);
-      case LTHC_DTYPE_BF16: return launch_pool1<__nv_bfloat16>(q, sms, s);
-      default: return launch_pool1<__half>(q, sms, s);
-    }
+  if (j.grad_w) {
+    const size_t need = wgrad_ws_bytes(j.B, j.G, j.C, j.L, sms);
+    if (!j.ws || ws_bytes < need)
+      return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", ws_bytes, need);
+    if (!aligned16(j.ws)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
   }
   switch (act) {
-    case LTHC_DTYPE_F32: return launch_pool_multi<float>(p, sms, s);
-    case LTHC_DTYPE_BF16: return launch_pool_multi<__nv_bfloat16>(p, sms, s);
-    default: return launch_pool_multi<__half>(p, sms, s);
+    case LTHC_DTYPE_F32: return read_family_t<float>(j, sms, s);
+    case LTHC_DTYPE_BF16: return read_family_t<__nv_bfloat16>(j, sms, s);
+    default: return read_family_t<__half>(j, sms, s);
   }
 }
 
@@ -490,7 +481,7 @@ int lthc_materialise12_fwd(const void* x0, const void* const* dz, const void* co
 
 size_t lthc_materialise_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C, int n_layers) {
   if (B <= 0 || G <= 0 || C <= 0 || n_layers < 1 || n_layers > kMaxLayers) return 0;
-  return wgrad_ws_bytes(B * G * G, C, n_layers, sms_for_sizing());
+  return wgrad_ws_bytes(B, G, C, n_layers, sms_for_sizing());
 }
 
 int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void* const* beta, int beta_dtype,
@@ -513,19 +504,9 @@ int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void
     LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
     for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (grad_beta) {
-    int sms = 0;
-    LTHC_TRY(current_device(&sms));
-    const size_t need = wgrad_ws_bytes(B * G * G, C, n_layers, sms);
-    if (B > 0 && (!workspace || workspace_bytes < need))
-      return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
-                  need);
-  }
-  if (grad_dz && B > 0) LTHC_TRY(pool_multi_impl(grad_out, beta, beta_dtype, n_layers, grad_dz, B, G, C, act_dtype, s));
-  if (grad_beta)
-    LTHC_TRY(weight_grad_impl(grad_out, dz, n_layers, grad_beta, workspace, workspace_bytes, B, G, C, act_dtype, s));
-  return LTHC_OK;
+  // One pass over grad_out produces both gradients.
+  ReadJob j{grad_out, beta, beta_dtype, grad_dz, dz, grad_beta, workspace, n_layers, B, G, C};
+  return read_family(j, workspace_bytes, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 size_t lthc_write_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
@@ -554,7 +535,8 @@ int lthc_read_fwd(const void* x, const void* alpha, int alpha_dtype, void* z, in
   if (B == 0) return LTHC_OK;
   const void* w[1] = {alpha};
   void* out[1] = {z};
-  return pool_multi_impl(x, w, alpha_dtype, 1, out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream));
+  ReadJob j{x, w, alpha_dtype, out, nullptr, nullptr, nullptr, 1, B, G, C};
+  return read_family(j, 0, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 size_t lthc_weight_grad_workspace_bytes(int64_t B, int64_t G, int64_t C, int n_layers) {
@@ -569,8 +551,8 @@ int lthc_weight_grad(const void* high, const void* const* low, int n_layers, flo
   LTHC_TRY(check_ptr(grad_w, "grad_w"));
   if (!low) return fail(LTHC_ERR_NULL_POINTER, "low pointer array is NULL");
   for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(low[l], "low[l]", B > 0));
-  return weight_grad_impl(high, low, n_layers, grad_w, workspace, workspace_bytes, B, G, C, act_dtype,
-                          static_cast<cudaStream_t>(stream));
+  ReadJob j{high, nullptr, LTHC_DTYPE_F32, nullptr, low, grad_w, workspace, n_layers, B, G, C};
+  return read_family(j, workspace_bytes, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
 size_t lthc_read_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
@@ -588,9 +570,10 @@ int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alph
   if (grad_alpha) LTHC_TRY(check_act(x, "x", B > 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (grad_alpha) {
+    // validate the workspace before anything is enqueued
     int sms = 0;
     LTHC_TRY(current_device(&sms));
-    const size_t need = wgrad_ws_bytes(B * G * G, C, 1, sms);
+    const size_t need = wgrad_ws_bytes(B, G, C, 1, sms);
     if (B > 0 && (!workspace || workspace_bytes < need))
       return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
                   need);
@@ -605,7 +588,8 @@ int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alph
   }
   if (grad_alpha) {
     const void* low[1] = {grad_z};
-    LTHC_TRY(weight_grad_impl(x, low, 1, grad_alpha, workspace, workspace_bytes, B, G, C, act_dtype, s));
+    ReadJob j{x, nullptr, LTHC_DTYPE_F32, nullptr, low, grad_alpha, workspace, 1, B, G, C};
+    LTHC_TRY(read_family(j, workspace_bytes, act_dtype, s));
   }
   return LTHC_OK;
 }
