@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=B_DEFAULT, help="images per GPU (BASELINE config 2: 64)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     p.add_argument("--no-extras", action="store_true", help="skip the per-kernel and comparator measurements")
+    p.add_argument("--op", default="materialise_fwd", choices=sorted(OPS),
+                   help="the LTHC op timed as the step (default: the BASELINE config 2 materialisation)")
     return p.parse_args()
 
 
@@ -158,6 +160,44 @@ def cpu_baseline(seconds: float) -> dict:
             "sample": f"{n} x materialise of B={Bs} (config 2 shapes, bf16) in {el:.1f} s on {O.num_threads()} threads"}
 
 
+# ------------------------------------------------------------------ ops
+def _op_inputs(B: int, dev, seed: int) -> dict:
+    cfg = W.config2(B=B, device=dev, seed=seed)
+    cfg["g"] = W.residual(B, G, C, seed=seed + 7, device=dev, dtype=torch.bfloat16)
+    cfg["alpha"] = torch.softmax(torch.randn(C, 16, device=dev, generator=torch.Generator(device=dev).manual_seed(seed)),
+                                 -1).to(torch.bfloat16)
+    cfg["z"] = torch.randn(B, G * G, C, device=dev, dtype=torch.bfloat16)
+    return cfg
+
+
+def op_step(op: str, cfg: dict):
+    """(step callable, algorithmic HBM bytes per step, kernel launches per step, kernel names)."""
+    from flowmatching_lthc_b200 import ops
+
+    B = cfg["B"]
+    x0, dz, P, g, alpha, z = cfg["x0"], cfg["dz"], cfg["P"], cfg["g"], cfg["alpha"], cfg["z"]
+    beta = P[0].to(torch.bfloat16)
+    table = {
+        "materialise_fwd": (lambda: ops.materialise(x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1,
+                            "broadcast_tma_kernel<bf16, 12, base>"),
+        "materialise_bwd": (lambda: ops.materialise_bwd(g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2), 2,
+                            "pool_tma_kernel<bf16, 12, pool, wgrad> + reduce_partials_kernel"),
+        "read_fwd": (lambda: ops.read(x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
+        "read_bwd": (lambda: ops.read_bwd(x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
+                     "broadcast_tma_kernel<bf16, 1> + pool_tma_kernel<bf16, 1, wgrad> + reduce_partials_kernel"),
+        "write_add_fwd": (lambda: ops.write_add(x0, dz[0], beta), W.write_add_bytes(B, G, C, 2, 2), 1,
+                          "broadcast_tma_kernel<bf16, 1, base>"),
+        "lazy_fwd": (lambda: ops.lazy_update(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 1,
+                     "lazy_fwd_kernel<bf16>"),
+        "lazy_bwd": (lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 2,
+                     "lazy_bwd_kernel<bf16> + lazy_bwd_finalize_kernel"),
+    }
+    return table[op]
+
+
+OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd")
+
+
 # ------------------------------------------------------------------ reference arm
 def reference_arm(args, r: D.Rank) -> int:
     if not r.is_main:
@@ -191,8 +231,19 @@ def reference_arm(args, r: D.Rank) -> int:
     return 0
 
 
-def config_dict(B: int, world: int) -> dict:
-    return {"workload": "materialise fwd X_L = X_0 + sum_l P_l(dZ_l), BASELINE config 2",
+WORKLOADS = {
+    "materialise_fwd": "materialise fwd X_L = X_0 + sum_l P_l(dZ_l), BASELINE config 2",
+    "materialise_bwd": "materialise bwd (grad dZ_l and grad P_l from grad X_L), config 2 shapes",
+    "read_fwd": "shared read Z = R(X_0), config 2 shapes",
+    "read_bwd": "read bwd (grad X_0 and grad alpha), config 2 shapes",
+    "write_add_fwd": "write_add X + P(dZ), config 2 shapes",
+    "lazy_fwd": "lazy update Z + Gamma*dZ, config 2 shapes",
+    "lazy_bwd": "lazy update bwd, config 2 shapes",
+}
+
+
+def config_dict(B: int, world: int, op: str = "materialise_fwd") -> dict:
+    return {"workload": WORKLOADS[op], "op": op,
             "global_batch": B * world, "batch_per_gpu": B, "residual": [B, 4 * G, 4 * G, C],
             "updates": [L, B, G * G, C], "act_dtype": "bf16", "weight_dtype": "fp32",
             "parallelism": f"dp{world} (batch-sharded replicas, no data-path collective)",
@@ -217,9 +268,8 @@ def main() -> int:
     stream = torch.cuda.current_stream(dev)
     B = args.batch
 
-    cfg = W.config2(B=B, device=dev, seed=1000 + r.rank)
-    x0, dz, P = cfg["x0"], cfg["dz"], cfg["P"]
-    step = lambda: ops.materialise(x0, dz, P)  # noqa: E731
+    cfg = _op_inputs(B, dev, seed=1000 + r.rank)
+    step, bytes_step, launches, kernel = op_step(args.op, cfg)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -244,19 +294,18 @@ def main() -> int:
         sampler.stop()
     clocks = sampler.summary(t_wall0, t_wall1, r.world) if sampler else None
 
-    bytes_step = W.materialise_bytes(B, G, C, L, 2)
     value = r.world * bytes_step * args.steps / (ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
-    kernel_ms = ms_local / args.steps  # one materialise launch per step
+    kernel_ms = ms_local / args.steps
     achieved = bytes_step / (kernel_ms / 1e3) / 1e9
-    traffic = ncu_traffic_per_launch()
+    traffic = ncu_traffic_per_launch() if args.op == "materialise_fwd" else None
     if traffic is not None and B != B_DEFAULT:
         traffic *= B / B_DEFAULT
 
     # end to end through the public operator: pinned host inputs -> device -> host result
     e2e = None
-    extras = {}
-    if r.is_main or r.world > 1:
+    if args.op == "materialise_fwd":
+        x0, dz, P = cfg["x0"], cfg["dz"], cfg["P"]
         h_x0 = x0.cpu().pin_memory()
         h_dz = [d.cpu().pin_memory() for d in dz]
         h_out = torch.empty_like(h_x0).pin_memory()
@@ -273,8 +322,7 @@ def main() -> int:
         e2e_step()
         torch.cuda.synchronize()
         n_e2e = max(3, min(args.steps, 10))
-        e2e_ms = time_device(e2e_step, n_e2e, stream)
-        e2e_ms = D.reduce_max(e2e_ms, dev)
+        e2e_ms = D.reduce_max(time_device(e2e_step, n_e2e, stream), dev)
         h2d = h_x0.numel() * 2 + sum(d.numel() * 2 for d in h_dz)
         e2e = {"value": round(r.world * bytes_step / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h_out.numel() * 2,
@@ -282,27 +330,28 @@ def main() -> int:
                "path": "pinned host buffers -> cudaMemcpyAsync -> lthc_b200::materialise (C ABI) -> host"}
         del h_x0, h_dz, h_out, d_x0, d_dz
 
+    extras = {}
     if r.world == 1 and not args.no_extras:
-        extras = measure_kernels(B, dev, stream, x0, dz, P, peak)
+        extras = measure_kernels(cfg, stream, peak)
 
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": r.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) residual, N(0,0.1) updates, N(0,0.02) fp32 weights; no dataset)",
-        "config": config_dict(B, r.world),
+        "config": config_dict(B, r.world, args.op),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "lthc::broadcast_kernel (materialise fwd)", "algorithmic_bytes_per_launch": bytes_step},
+                     "kernel": kernel, "algorithmic_bytes_per_launch": bytes_step},
         "cpu_baseline": None,
         "e2e": e2e,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches,
         "clocks": clocks,
     }
     if extras:
         line["kernels"] = extras.get("kernels")
         line["comparators"] = extras.get("comparators")
-    if r.is_main and r.world == 1:
+    if r.is_main and r.world == 1 and args.op == "materialise_fwd":
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if r.is_main:
         print(json.dumps(line), flush=True)
@@ -311,35 +360,21 @@ def main() -> int:
     return 0
 
 
-def measure_kernels(B, dev, stream, x0, dz, P, peak) -> dict:
-    """Device-timed GB/s of every LTHC kernel at B=64 bf16 (informational; not the
+def measure_kernels(cfg: dict, stream, peak) -> dict:
+    """Device-timed GB/s of every LTHC op at B=64 bf16 (informational; not the
     headline), plus the reference's Triton ops on the same inputs when the
     reference package is installed under baseline/_ref."""
-    from flowmatching_lthc_b200 import ops
-
     out: dict = {"kernels": {}, "comparators": {}}
     iters = 20
-    alpha = torch.softmax(torch.randn(C, 16, device=dev), -1).to(torch.bfloat16)
-    g = W.residual(B, G, C, seed=7, device=dev, dtype=torch.bfloat16)
-    z = torch.randn(B, G * G, C, device=dev, dtype=torch.bfloat16)
-    beta_bf = P[0].to(torch.bfloat16)
-
-    def rec(name, fn, nbytes, launches):
+    for op in OPS:
+        fn, nbytes, launches, _ = op_step(op, cfg)
         fn()
         ms = time_device(fn, iters, stream)
-        out["kernels"][name] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
-                                "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4), "bytes": nbytes,
-                                "launches": launches}
+        out["kernels"][op] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                              "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4), "bytes": nbytes,
+                              "launches": launches}
 
-    rec("materialise_fwd", lambda: ops.materialise(x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1)
-    rec("materialise_bwd", lambda: ops.materialise_bwd(g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2),
-        3)
-    rec("read_fwd", lambda: ops.read(x0, alpha), W.read_bytes(B, G, C, 2, 2), 1)
-    rec("write_add_fwd", lambda: ops.write_add(x0, dz[0], beta_bf), W.write_add_bytes(B, G, C, 2, 2), 1)
-    rec("lazy_update_fwd", lambda: ops.lazy_update(z, dz[0], alpha, beta_bf), W.lazy_bytes(B * G * G, C, 2, 2), 1)
-    rec("read_bwd", lambda: ops.read_bwd(x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3)
-    rec("lazy_update_bwd", lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta_bf), W.lazy_bytes(B * G * G, C, 2, 2), 2)
-
+    B, x0, dz, P, g = cfg["B"], cfg["x0"], cfg["dz"], cfg["P"], cfg["g"]
     ref = ROOT / "baseline" / "_ref"
     if (ref / "flowmatching_lthc").exists():
         try:

@@ -127,11 +127,6 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 int64_t slices_of(int64_t C) { return ceil_div(C, kSliceCh); }
 
 // ---- grid plans (pure functions of the problem size and the SM count) ------
-int64_t plan_grid_stride(int64_t rows, int64_t C, int sms, int per_sm, int rows_per_block) {
-  const int64_t slices = slices_of(C);
-  int64_t bx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
-  return std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(rows, rows_per_block)));
-}
 
 // Weight-gradient partials: one [L][C][16] fp32 block per CTA column of the read
 // kernel, whose grid is fixed at two CTAs per SM so that the workspace size is a
@@ -140,21 +135,35 @@ constexpr int kWgradCtasPerSm = 2;
 
 int64_t strips_of(int64_t B, int64_t G) { return B * G * ceil_div(G, kStripCells); }
 
-int64_t wgrad_blocks(int64_t strips, int64_t C, int sms) {
-  const int64_t nx = std::max<int64_t>(1, std::min<int64_t>(ceil_div(static_cast<int64_t>(sms) * kWgradCtasPerSm,
-                                                                     slices_of(C)),
-                                                            strips));
+// CTA columns for `per_sm` resident CTAs per SM: rounded down so that the whole
+// grid (columns x channel slices) fits in one wave.
+int64_t one_wave_columns(int64_t strips, int64_t C, int sms, int per_sm) {
+  const int64_t nx = std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(sms) * per_sm / slices_of(C), strips));
   return ceil_div(strips, ceil_div(strips, nx));
 }
+
+int64_t wgrad_blocks(int64_t strips, int64_t C, int sms) { return one_wave_columns(strips, C, sms, kWgradCtasPerSm); }
 
 size_t wgrad_ws_bytes(int64_t B, int64_t G, int64_t C, int L, int sms) {
   if (B <= 0) return 0;
   return static_cast<size_t>(wgrad_blocks(strips_of(B, G), C, sms)) * L * C * kPos * sizeof(float);
 }
 
+// Lazy-update grid: CTAs of 8 warps over (row blocks) x (channel slices of 32
+// 16-byte vectors).  The fp32 slice (128 channels) is the narrowest, so the row
+// block count below is an upper bound for every dtype; the partial buffer is
+// sized with it.
+int64_t lazy_slices(int64_t C, int esize) { return ceil_div(C, 32 * (16 / esize)); }
+
+int64_t lazy_row_blocks(int64_t N, int64_t C, int sms) {
+  const int64_t slices = lazy_slices(C, 4);
+  const int64_t bx = std::max<int64_t>(1, static_cast<int64_t>(sms) * 4 / slices);
+  return std::max<int64_t>(1, std::min<int64_t>(bx, ceil_div(N, kLazyWarps)));
+}
+
 size_t lazy_ws_bytes(int64_t N, int64_t C, int sms) {
   if (N <= 0) return 0;
-  return static_cast<size_t>(plan_grid_stride(N, C, sms, 4, kLazyWarps)) * C * sizeof(float);
+  return static_cast<size_t>(lazy_row_blocks(N, C, sms)) * C * sizeof(float);
 }
 
 // ---- TMA tensor maps ---------------------------------------------------------
@@ -172,6 +181,13 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
+#ifndef LTHC_L2_PROMOTION
+#define LTHC_L2_PROMOTION 0  // 0 none, 1 128 B, 2 256 B
+#endif
+constexpr CUtensorMapL2promotion kL2Promotion =
+    LTHC_L2_PROMOTION == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                           : (LTHC_L2_PROMOTION == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+
 template <typename T>
 CUtensorMapDataType tmap_dtype() {
   if constexpr (sizeof(T) == 4) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -179,8 +195,8 @@ CUtensorMapDataType tmap_dtype() {
   else return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-// NHWC residual [B, 4G, 4G, C] as a 4-D map (C, W, H, B); box = 64 channels x 16
-// columns x 4 rows x 1 image (one strip of 4 cells).
+// NHWC residual [B, 4G, 4G, C] as a 4-D map (C, W, H, B); box = 64 channels x
+// 4*kStripCells columns x 4 rows x 1 image (one strip of cells).
 template <typename T>
 int encode_residual_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t G, int64_t C) {
   auto enc = tmap_encoder();
@@ -189,16 +205,16 @@ int encode_residual_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t G, i
   const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(4 * G),
                               static_cast<cuuint64_t>(4 * G), static_cast<cuuint64_t>(B)};
   const cuuint64_t strides[3] = {C * es, 4 * G * C * es, 16 * G * G * C * es};
-  const cuuint32_t box[4] = {kSliceCh, 16, 4, 1};
+  const cuuint32_t box[4] = {kSliceCh, kBoxCols, 4, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, tmap_dtype<T>(), 4, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, kL2Promotion,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (residual) failed with %d", (int)r);
   return LTHC_OK;
 }
 
-// Workspace [rows, C] as a 2-D map; box = 64 channels x 4 rows (one strip).
+// Workspace [rows, C] as a 2-D map; box = 64 channels x kStripCells rows (one strip).
 template <typename T>
 int encode_workspace_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t C) {
   auto enc = tmap_encoder();
@@ -209,7 +225,7 @@ int encode_workspace_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t 
   const cuuint32_t box[2] = {kSliceCh, kStripCells};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, tmap_dtype<T>(), 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, kL2Promotion,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (workspace) failed with %d", (int)r);
   return LTHC_OK;
@@ -246,8 +262,7 @@ int launch_broadcast_tma(BcastTmaParams& p, int sms, cudaStream_t s) {
   int per_sm = 1;
   LTHC_TRY(resident_ctas(kern, kBcastThreads, Lay::kSmemBytes, &per_sm));
   const int64_t slices = slices_of(p.C);
-  int64_t nx = ceil_div(static_cast<int64_t>(sms) * per_sm, slices);
-  nx = std::max<int64_t>(1, std::min<int64_t>(nx, p.strips));
+  int64_t nx = one_wave_columns(p.strips, p.C, sms, per_sm);
   p.strips_per_cta = ceil_div(p.strips, nx);
   nx = ceil_div(p.strips, p.strips_per_cta);
   kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), kBcastThreads, Lay::kSmemBytes, s>>>(p);
@@ -260,6 +275,7 @@ int broadcast_t(const void* base, const void* const* dz, const void* const* w, i
   BcastTmaParams p;
   memset(&p, 0, sizeof(p));
   if (base) LTHC_TRY(encode_residual_map<T>(&p.tm_base, base, B, G, C));
+  LTHC_TRY(encode_residual_map<T>(&p.tm_out, out, B, G, C));
   for (int l = 0; l < L; ++l) {
     LTHC_TRY(encode_workspace_map<T>(&p.tm_dz[l], dz[l], B * G * G, C));
     p.w[l] = w[l];
@@ -309,9 +325,7 @@ int launch_read_t(PoolTmaParams& p, float* grad_w, int sms, cudaStream_t s) {
   int per_sm = 1;
   LTHC_TRY(resident_ctas(kern, Lay::kThreads, Lay::kSmemBytes, &per_sm));
   const int64_t slices = slices_of(p.C);
-  int64_t nx = WGRAD ? wgrad_blocks(p.strips, p.C, sms)
-                     : std::max<int64_t>(1, std::min<int64_t>(ceil_div(static_cast<int64_t>(sms) * per_sm, slices),
-                                                              p.strips));
+  int64_t nx = WGRAD ? wgrad_blocks(p.strips, p.C, sms) : one_wave_columns(p.strips, p.C, sms, per_sm);
   p.strips_per_cta = ceil_div(p.strips, nx);
   nx = ceil_div(p.strips, p.strips_per_cta);
   kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), Lay::kThreads, Lay::kSmemBytes, s>>>(p);
@@ -618,7 +632,8 @@ int lthc_lazy_update_fwd(const void* z, const void* dz, const void* alpha, int a
   int sms = 0;
   LTHC_TRY(current_device(&sms));
   LazyParams p{z, dz, alpha, beta, z_out, nullptr, alpha_dtype, beta_dtype, N, C};
-  dim3 grid(static_cast<unsigned>(plan_grid_stride(N, C, sms, 4, kLazyWarps)), static_cast<unsigned>(slices_of(C)));
+  const int es = act_dtype == LTHC_DTYPE_F32 ? 4 : 2;
+  dim3 grid(static_cast<unsigned>(lazy_row_blocks(N, C, sms)), static_cast<unsigned>(lazy_slices(C, es)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (act_dtype) {
     case LTHC_DTYPE_F32: lazy_fwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
@@ -660,9 +675,10 @@ int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alp
     return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
                 need);
   if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
-  const int64_t nblk = plan_grid_stride(N, C, sms, 4, kLazyWarps);
+  const int64_t nblk = lazy_row_blocks(N, C, sms);
   LazyParams p{grad_z_out, dz, alpha, beta, grad_dz, static_cast<float*>(workspace), alpha_dtype, beta_dtype, N, C};
-  dim3 grid(static_cast<unsigned>(nblk), static_cast<unsigned>(slices_of(C)));
+  const int es = act_dtype == LTHC_DTYPE_F32 ? 4 : 2;
+  dim3 grid(static_cast<unsigned>(nblk), static_cast<unsigned>(lazy_slices(C, es)));
   switch (act_dtype) {
     case LTHC_DTYPE_F32: lazy_bwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
     case LTHC_DTYPE_BF16: lazy_bwd_kernel<__nv_bfloat16><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;

@@ -3,16 +3,17 @@
 // backward's grad_x).
 //
 // CTA = 4 consumer warps + 1 producer warp, owning one 64-channel slice of the
-// residual.  The producer's elected lane streams "strips" of 4 horizontally
-// adjacent cells into a ring of shared-memory stages with TMA:
-//   base tile  [4 rows][16 columns][64 channels]   (box of the NHWC residual)
+// residual.  The producer's elected lane streams "strips" of kStripCells
+// horizontally adjacent cells into a ring of shared-memory stages with TMA:
+//   base tile  [4 rows][4*strip columns][64 channels] (box of the NHWC residual)
 //   dz tiles   [L][4 cells][64 channels]           (box of each workspace update)
 // Consumer warp `row` owns cell row `row`; lane l owns channel pair (2l, 2l+1)
 // and keeps w_l[c, 4*row + col] for all L layers and 4 columns in registers, so
 // each weight is loaded once per CTA.  Per cell a lane reads 4 base pairs and
 // L update pairs from shared memory (128 contiguous bytes per warp access, no
 // bank conflicts), accumulates in fp32 with packed fp32x2 FMAs in the order
-// base, l = 0, 1, ... and stores 4 pairs with streaming stores.
+// base, l = 0, 1, ... and writes the rounded result back over the base tile,
+// which one TMA store per strip then writes to the output.
 // Full/empty mbarriers hand stages between producer and consumers; every wait
 // is bounded (lthc_tma.cuh).
 #pragma once
@@ -22,22 +23,33 @@
 
 namespace lthc {
 
-constexpr int kStripCells = 4;
+// Pipeline shape.  A strip is kStripCells horizontally adjacent cells (its
+// residual box spans 4 * kStripCells token columns); 16-bit activations use
+// LTHC_STAGES_16BIT shared-memory stages per CTA, fp32 half as many.
+#ifndef LTHC_STRIP_CELLS
+#define LTHC_STRIP_CELLS 4
+#endif
+#ifndef LTHC_STAGES_16BIT
+#define LTHC_STAGES_16BIT 4
+#endif
+constexpr int kStripCells = LTHC_STRIP_CELLS;
+constexpr int kBoxCols = 4 * kStripCells;
 constexpr int kBcastConsumerWarps = 4;
 constexpr int kBcastThreads = 32 * (kBcastConsumerWarps + 1);
 
 template <typename T, int LMAX>
 struct BcastLayout {
-  static constexpr int kBaseBytes = 4 * 16 * kSliceCh * static_cast<int>(sizeof(T));
+  static constexpr int kBaseBytes = 4 * kBoxCols * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kDzTileBytes = kStripCells * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kStageBytes = kBaseBytes + LMAX * kDzTileBytes;
-  static constexpr int kStages = sizeof(T) == 2 ? 4 : 2;
+  static constexpr int kStages = sizeof(T) == 2 ? LTHC_STAGES_16BIT : (LTHC_STAGES_16BIT + 1) / 2;
   static constexpr int kBarrierOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarrierOffset + 2 * kStages * 8 + 128;  // + alignment slack
 };
 
 struct BcastTmaParams {
   CUtensorMap tm_base;                 // 4D (C, 4G, 4G, B) box (64, 16, 4, 1); unused without a base
+  CUtensorMap tm_out;                  // 4D map of the output, same box
   CUtensorMap tm_dz[kMaxLayers];       // 2D (C, B*G*G) box (64, 4)
   const void* w[kMaxLayers];           // [C, 16] weights, dtype w_dtype
   void* out;                           // T[B, 4G, 4G, C]
@@ -50,13 +62,33 @@ struct BcastTmaParams {
   int64_t strips_per_cta;
 };
 
-__device__ __forceinline__ void strip_coords(int64_t strip, int G, int spr, int64_t& b, int& wy, int& wx0) {
-  const int64_t per_img = static_cast<int64_t>(G) * spr;
-  b = strip / per_img;
-  const int rem = static_cast<int>(strip - b * per_img);
-  wy = rem / spr;
-  wx0 = (rem - wy * spr) * kStripCells;
-}
+// Position of a strip: image b, cell row wy, first cell column wx0.  A CTA walks
+// consecutive strips, so the cursor advances with adds and compares only (the
+// 64-bit division happens once, when the cursor is created).
+struct StripCursor {
+  int64_t b;
+  int wy;
+  int sx;   // strip index inside the cell row
+  int G;
+  int spr;  // strips per cell row
+  __device__ __forceinline__ StripCursor(int64_t strip, int G_, int spr_) : G(G_), spr(spr_) {
+    const int64_t per_img = static_cast<int64_t>(G_) * spr_;
+    b = strip / per_img;
+    const int rem = static_cast<int>(strip - b * per_img);
+    wy = rem / spr_;
+    sx = rem - wy * spr_;
+  }
+  __device__ __forceinline__ int wx0() const { return sx * kStripCells; }
+  __device__ __forceinline__ void next() {
+    if (++sx == spr) {
+      sx = 0;
+      if (++wy == G) {
+        wy = 0;
+        ++b;
+      }
+    }
+  }
+};
 
 template <typename T, int LT, bool HAS_BASE>
 __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const __grid_constant__ BcastTmaParams p) {
@@ -78,7 +110,7 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
   if (threadIdx.x == 0) {
     for (int s = 0; s < Lay::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kBcastConsumerWarps);
+      mbar_init(&empty[s], 1);  // released by the thread that stores the stage's output tile
     }
     fence_barrier_init();
   }
@@ -94,13 +126,13 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
       const uint32_t tx = (HAS_BASE ? Lay::kBaseBytes : 0) + static_cast<uint32_t>(L) * Lay::kDzTileBytes;
       const int64_t GG = static_cast<int64_t>(p.G) * p.G;
       int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
+      StripCursor cur(s_begin, p.G, p.strips_per_row);
+      for (int it = 0; it < n_it; ++it, cur.next()) {
         const int s = it % Lay::kStages;
         const uint32_t ph = (it / Lay::kStages) & 1;
         if (it >= Lay::kStages && !mbar_wait(&empty[s], ph ^ 1)) break;
-        int64_t b;
-        int wy, wx0;
-        strip_coords(s_begin + it, p.G, p.strips_per_row, b, wy, wx0);
+        const int64_t b = cur.b;
+        const int wy = cur.wy, wx0 = cur.wx0();
         uint8_t* st = smem + s * Lay::kStageBytes;
         mbar_arrive_expect_tx(&full[s], tx);
         if constexpr (HAS_BASE)
@@ -122,6 +154,10 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
   }
 
   // ---------------- consumers ---------------------------------------------------
+  // Each lane computes its 4 columns x cells of the strip in place over the staged
+  // base tile; then one elected thread writes the whole tile with a TMA store
+  // (which clips columns past the residual edge and channels past C) and hands
+  // the stage back to the producer once the store has read it.
   const int row = warp;
   const int64_t c = c0 + 2 * lane;
   const bool cvalid = c < p.C;
@@ -138,49 +174,48 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
       }
     }
   }
-  T* out = static_cast<T*>(p.out);
-  const int64_t H = 4 * static_cast<int64_t>(p.G);
   const uint32_t smem_base = smem_u32(smem);
   constexpr uint32_t kEs = sizeof(T);
+  const bool storer = warp == 0 && lane == 0;
+  StripCursor cur(s_begin, p.G, p.strips_per_row);
 
-  for (int it = 0; it < n_it; ++it) {
+  for (int it = 0; it < n_it; ++it, cur.next()) {
     const int s = it % Lay::kStages;
     if (!mbar_wait(&full[s], (it / Lay::kStages) & 1)) break;
-    int64_t b;
-    int wy, wx0;
-    strip_coords(s_begin + it, p.G, p.strips_per_row, b, wy, wx0);
     const uint32_t sb = smem_base + s * Lay::kStageBytes;
-    const int ncell = min(kStripCells, p.G - wx0);
-    if (cvalid) {
-      const int64_t tok_row = ((b * H + 4 * wy + row) * H + 4 * wx0) * p.C + c;
 #pragma unroll
-      for (int k = 0; k < kStripCells; ++k) {
-        if (k < ncell) {
-          float2 acc[4];
+    for (int k = 0; k < kStripCells; ++k) {
+      float2 acc[4];
+      const uint32_t xa = sb + ((row * kBoxCols + 4 * k) * kSliceCh + 2 * lane) * kEs;
 #pragma unroll
-          for (int col = 0; col < 4; ++col) {
-            if constexpr (HAS_BASE)
-              acc[col] = lds_pair<T>(sb + ((row * 16 + 4 * k + col) * kSliceCh + 2 * lane) * kEs);
-            else
-              acc[col] = make_float2(0.f, 0.f);
-          }
+      for (int col = 0; col < 4; ++col) {
+        if constexpr (HAS_BASE)
+          acc[col] = lds_pair<T>(xa + col * kSliceCh * kEs);
+        else
+          acc[col] = make_float2(0.f, 0.f);
+      }
 #pragma unroll
-          for (int l = 0; l < LMAX; ++l) {
-            if (l < L) {
-              const float2 d = lds_pair<T>(sb + Lay::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
+      for (int l = 0; l < LMAX; ++l) {
+        if (l < L) {
+          const float2 d = lds_pair<T>(sb + Lay::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-              for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
-            }
-          }
-          T* dst = out + tok_row + static_cast<int64_t>(4 * k) * p.C;
-#pragma unroll
-          for (int col = 0; col < 4; ++col) Act<T>::st_stream(dst + col * p.C, acc[col]);
+          for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
         }
       }
+#pragma unroll
+      for (int col = 0; col < 4; ++col) sts_pair<T>(xa + col * kSliceCh * kEs, acc[col]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    fence_proxy_async_smem();
+    named_barrier(1, 32 * kBcastConsumerWarps);
+    if (storer) {
+      tma_store_4d(&p.tm_out, smem + s * Lay::kStageBytes, static_cast<int32_t>(c0), 4 * cur.wx0(), 4 * cur.wy,
+                   static_cast<int32_t>(cur.b));
+      bulk_commit();
+      bulk_wait_read<1>();  // the previous stage's store has read its tile
+      if (it > 0) mbar_arrive(&empty[(it - 1) % Lay::kStages]);
+    }
   }
+  if (storer) bulk_wait_all();
 }
 
 }  // namespace lthc

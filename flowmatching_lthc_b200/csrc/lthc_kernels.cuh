@@ -24,7 +24,10 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
 
 // ---------------------------------------------------------------------------
 // lazy workspace recurrence: z_out = z + gamma (.) dz, gamma[c] = sum_r a[c,r] b[c,r]
-// gamma is recomputed per thread from the two weight rows (32 fp32 FMAs).
+// Lane = one 16-byte vector of V = 16/sizeof(T) channels; a warp covers a slice
+// of 32*V channels of one workspace row (blockIdx.y = slice), the 8 warps of a
+// CTA walk rows.  gamma of the slice is computed once per CTA (fp32 FMAs in
+// position order) into shared memory.
 // ---------------------------------------------------------------------------
 struct LazyParams {
   const void* z;        // fwd: z ; bwd: grad_z_out
@@ -41,24 +44,72 @@ struct LazyParams {
 
 constexpr int kLazyWarps = 8;
 
-__device__ __forceinline__ float2 gamma_pair(const LazyParams& p, int64_t c) {
-  float2 g = make_float2(0.f, 0.f);
+template <typename T>
+struct Vec16 {
+  static constexpr int V = 16 / sizeof(T);   // channels per 16-byte vector
+  static constexpr int kSlice = 32 * V;      // channels per warp
+};
+
+template <typename T>
+__device__ __forceinline__ void lazy_gamma_slice(const LazyParams& p, int64_t cbase, float* g_s) {
+  for (int i = threadIdx.x; i < Vec16<T>::kSlice; i += blockDim.x) {
+    const int64_t c = cbase + i;
+    float g = 0.f;
+    if (c < p.C) {
 #pragma unroll
-  for (int r = 0; r < kPos; ++r) {
-    g.x = fmaf(load_weight(p.a, p.a_dtype, c * kPos + r), load_weight(p.b, p.b_dtype, c * kPos + r), g.x);
-    g.y = fmaf(load_weight(p.a, p.a_dtype, (c + 1) * kPos + r), load_weight(p.b, p.b_dtype, (c + 1) * kPos + r),
-               g.y);
+      for (int r = 0; r < kPos; ++r)
+        g = fmaf(load_weight(p.a, p.a_dtype, c * kPos + r), load_weight(p.b, p.b_dtype, c * kPos + r), g);
+    }
+    g_s[i] = g;
   }
-  return g;
+  __syncthreads();
+}
+
+// 16-byte vector of T as V floats
+template <typename T>
+__device__ __forceinline__ void ld_vec(const T* p, float (&v)[Vec16<T>::V]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(w[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Act<T>::cvt(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void st_vec(T* p, const float (&v)[Vec16<T>::V]) {
+  uint4 raw;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&raw);
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = __float_as_uint(v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = Act<T>::pack(make_float2(v[2 * i], v[2 * i + 1]));
+  }
+  *reinterpret_cast<uint4*>(p) = raw;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256) lazy_fwd_kernel(const __grid_constant__ LazyParams p) {
+  constexpr int V = Vec16<T>::V;
+  __shared__ float g_s[Vec16<T>::kSlice];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t c = static_cast<int64_t>(blockIdx.y) * kSliceCh + 2 * lane;
+  const int64_t cbase = static_cast<int64_t>(blockIdx.y) * Vec16<T>::kSlice;
+  lazy_gamma_slice<T>(p, cbase, g_s);
+  const int64_t c = cbase + lane * V;
   if (c >= p.C) return;
-  const float2 g = gamma_pair(p, c);
+  float g[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) g[i] = g_s[lane * V + i];
   const T* z = static_cast<const T*>(p.z);
   const T* dz = static_cast<const T*>(p.dz);
   T* out = static_cast<T*>(p.out);
@@ -66,22 +117,37 @@ __global__ void __launch_bounds__(256) lazy_fwd_kernel(const __grid_constant__ L
   for (int64_t n = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n < p.N;
        n += static_cast<int64_t>(gridDim.x) * kLazyWarps) {
     const int64_t off = n * p.C + c;
-    const float2 zv = Act<T>::cvt(Act<T>::ld(z + off));
-    const float2 dv = Act<T>::cvt(Act<T>::ld(dz + off));
-    Act<T>::st(out + off, ffma2(g, dv, zv));
+    float zv[V], dv[V];
+    ld_vec<T>(z + off, zv);
+    ld_vec<T>(dz + off, dv);
+#pragma unroll
+    for (int i = 0; i < V; i += 2) {
+      const float2 r = ffma2(make_float2(g[i], g[i + 1]), make_float2(dv[i], dv[i + 1]), make_float2(zv[i], zv[i + 1]));
+      zv[i] = r.x;
+      zv[i + 1] = r.y;
+    }
+    st_vec<T>(out + off, zv);
   }
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256) lazy_bwd_kernel(const __grid_constant__ LazyParams p) {
-  __shared__ float2 red[kLazyWarps][32];
+  constexpr int V = Vec16<T>::V;
+  __shared__ float g_s[Vec16<T>::kSlice];
+  __shared__ float red[kLazyWarps][Vec16<T>::kSlice];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t c = static_cast<int64_t>(blockIdx.y) * kSliceCh + 2 * lane;
+  const int64_t cbase = static_cast<int64_t>(blockIdx.y) * Vec16<T>::kSlice;
+  lazy_gamma_slice<T>(p, cbase, g_s);
+  const int64_t c = cbase + lane * V;
   const bool valid = c < p.C;
-  float2 acc = make_float2(0.f, 0.f);
+  float acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = 0.f;
   if (valid) {
-    const float2 g = gamma_pair(p, c);
+    float g[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) g[i] = g_s[lane * V + i];
     const T* gz = static_cast<const T*>(p.z);
     const T* dz = static_cast<const T*>(p.dz);
     T* gdz = static_cast<T*>(p.out);
@@ -89,21 +155,33 @@ __global__ void __launch_bounds__(256) lazy_bwd_kernel(const __grid_constant__ L
     for (int64_t n = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n < p.N;
          n += static_cast<int64_t>(gridDim.x) * kLazyWarps) {
       const int64_t off = n * p.C + c;
-      const float2 gv = Act<T>::cvt(Act<T>::ld(gz + off));
-      const float2 dv = Act<T>::cvt(Act<T>::ld(dz + off));
-      Act<T>::st(gdz + off, fmul2(g, gv));
-      acc = ffma2(gv, dv, acc);
+      float gv[V], dv[V], o[V];
+      ld_vec<T>(gz + off, gv);
+      ld_vec<T>(dz + off, dv);
+#pragma unroll
+      for (int i = 0; i < V; i += 2) {
+        const float2 m = fmul2(make_float2(g[i], g[i + 1]), make_float2(gv[i], gv[i + 1]));
+        o[i] = m.x;
+        o[i + 1] = m.y;
+        const float2 a2 = ffma2(make_float2(gv[i], gv[i + 1]), make_float2(dv[i], dv[i + 1]),
+                                make_float2(acc[i], acc[i + 1]));
+        acc[i] = a2.x;
+        acc[i + 1] = a2.y;
+      }
+      st_vec<T>(gdz + off, o);
     }
   }
-  red[warp][lane] = acc;
-  __syncthreads();
-  if (warp == 0 && valid) {
-    float2 s = red[0][lane];
 #pragma unroll
-    for (int w = 1; w < kLazyWarps; ++w) s = fadd2(s, red[w][lane]);
-    float* P = p.partial + static_cast<int64_t>(blockIdx.x) * p.C;
-    P[c] = s.x;
-    P[c + 1] = s.y;
+  for (int i = 0; i < V; ++i) red[warp][lane * V + i] = acc[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < Vec16<T>::kSlice; i += blockDim.x) {
+    const int64_t cc = cbase + i;
+    if (cc < p.C) {
+      float s = red[0][i];
+#pragma unroll
+      for (int w = 1; w < kLazyWarps; ++w) s += red[w][i];
+      p.partial[static_cast<int64_t>(blockIdx.x) * p.C + cc] = s;
+    }
   }
 }
 

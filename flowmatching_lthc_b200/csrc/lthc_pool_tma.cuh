@@ -7,15 +7,15 @@
 // low = dz_l), so grad X_L is read from HBM exactly once.
 //
 // CTA roles (one 64-channel slice, lane = channel pair):
-//   warps [0, 4)            WGRAD: warp = cell row; each lane keeps 4 columns x L
-//                           layers x 2 channels of fp32 accumulators in registers
+//   WGRAD warps             4 cell rows x layer groups; each lane keeps 4 columns x
+//                           its layers x 2 channels of fp32 accumulators in registers
 //   next POOL_WARPS warps   POOL: each owns CELLS_PER_POOL cells of the strip and
 //                           reads the weights from a shared-memory copy laid out
 //                           [r][layer pair][lane] as float4 (one 16-byte load
 //                           feeds two layers, conflict-free)
 //   last warp               producer (one elected lane issues the TMA loads)
-// A strip is 4 horizontally adjacent cells; stages hold the H tile
-// [4 rows][16 columns][64 channels] and, for WGRAD, the L low tiles
+// A strip is kStripCells horizontally adjacent cells; stages hold the H tile
+// [4 rows][4*kStripCells columns][64 channels] and, for WGRAD, the L low tiles
 // [L][4 cells][64 channels].  Sums run in fp32 in position order r = 0..15
 // (POOL) and strip order (WGRAD); WGRAD partials are per CTA and reduced later
 // in CTA order, so the result is bitwise reproducible.
@@ -27,17 +27,50 @@
 
 namespace lthc {
 
-constexpr int kWgradWarps = 4;
+// Weight-gradient warps: 4 cell rows x WGRAD layer groups (the accumulators of
+// a deep update stack are split across warps so that every warp of the CTA
+// stays near 80 registers).
+#ifndef LTHC_WGRAD_LAYERS_PER_WARP
+#define LTHC_WGRAD_LAYERS_PER_WARP 12
+#endif
+
+template <int LMAX>
+constexpr int wgrad_layer_groups() {
+  return LMAX <= 2 ? 1 : (LMAX + LTHC_WGRAD_LAYERS_PER_WARP - 1) / LTHC_WGRAD_LAYERS_PER_WARP;
+}
+
+// Layers per pooling warp for the deep (L = 12) variants; the pooling work of a
+// strip is split across warps by layer group so that no warp is the critical path.
+#ifndef LTHC_POOL_LAYERS_PER_WARP
+#define LTHC_POOL_LAYERS_PER_WARP 4
+#endif
+
+// Positions of the pooling loop that are unrolled together (loads of the next
+// position overlap the FMAs of the current one).
+#ifndef LTHC_POOL_UNROLL
+#define LTHC_POOL_UNROLL 4
+#endif
+constexpr int kPoolUnroll = LTHC_POOL_UNROLL;
+
+template <int LMAX>
+constexpr int pool_layer_groups() {
+  return LMAX <= 2 ? 1 : (LMAX + LTHC_POOL_LAYERS_PER_WARP - 1) / LTHC_POOL_LAYERS_PER_WARP;
+}
 
 template <typename T, int LMAX, bool POOL, bool WGRAD, int CELLS_PER_POOL>
 struct PoolLayout {
-  static constexpr int kPoolWarps = POOL ? kStripCells / CELLS_PER_POOL : 0;
-  static constexpr int kConsumerWarps = (WGRAD ? kWgradWarps : 0) + kPoolWarps;
+  static constexpr int kLayerGroups = pool_layer_groups<LMAX>();
+  static constexpr int kGroupPairs = ((LMAX + 1) / 2 + kLayerGroups - 1) / kLayerGroups;  // layer pairs per warp
+  static constexpr int kPoolWarps = POOL ? (kStripCells / CELLS_PER_POOL) * kLayerGroups : 0;
+  static constexpr int kWgradGroups = wgrad_layer_groups<LMAX>();
+  static constexpr int kWgradLayers = (LMAX + kWgradGroups - 1) / kWgradGroups;  // layers per WGRAD warp
+  static constexpr int kWgradWarps = WGRAD ? 4 * kWgradGroups : 0;
+  static constexpr int kConsumerWarps = kWgradWarps + kPoolWarps;
   static constexpr int kThreads = 32 * (kConsumerWarps + 1);
-  static constexpr int kHBytes = 4 * 16 * kSliceCh * static_cast<int>(sizeof(T));
+  static constexpr int kHBytes = 4 * kBoxCols * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kLowTileBytes = kStripCells * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kStageBytes = kHBytes + (WGRAD ? LMAX * kLowTileBytes : 0);
-  static constexpr int kStages = sizeof(T) == 2 ? 4 : 2;
+  static constexpr int kStages = sizeof(T) == 2 ? LTHC_STAGES_16BIT : (LTHC_STAGES_16BIT + 1) / 2;
   static constexpr int kLayerPairs = (LMAX + 1) / 2;
   static constexpr int kWBytes = POOL ? kPos * kLayerPairs * 32 * 16 : 0;  // [r][lp][lane] float4
   static constexpr int kWOffset = kStages * kStageBytes;
@@ -67,12 +100,12 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr) {
 }
 
 template <typename T, int LT, bool POOL, bool WGRAD, int CELLS_PER_POOL>
-__global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL, WGRAD, CELLS_PER_POOL>::kThreads, 1)
+__global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL, WGRAD, CELLS_PER_POOL>::kThreads, 2)
     pool_tma_kernel(const __grid_constant__ PoolTmaParams p) {
   constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
   using Lay = PoolLayout<T, LMAX, POOL, WGRAD, CELLS_PER_POOL>;
   constexpr int kProducerWarp = Lay::kConsumerWarps;
-  constexpr int kPoolWarp0 = WGRAD ? kWgradWarps : 0;
+  constexpr int kPoolWarp0 = Lay::kWgradWarps;
   constexpr uint32_t kEs = sizeof(T);
 
   extern __shared__ uint8_t smem_raw[];
@@ -132,13 +165,13 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
       const uint32_t tx = Lay::kHBytes + (WGRAD ? static_cast<uint32_t>(L) * Lay::kLowTileBytes : 0u);
       const int64_t GG = static_cast<int64_t>(p.G) * p.G;
       int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
+      StripCursor cur(s_begin, p.G, p.strips_per_row);
+      for (int it = 0; it < n_it; ++it, cur.next()) {
         const int s = it % Lay::kStages;
         const uint32_t ph = (it / Lay::kStages) & 1;
         if (it >= Lay::kStages && !mbar_wait(&empty[s], ph ^ 1)) break;
-        int64_t b;
-        int wy, wx0;
-        strip_coords(s_begin + it, p.G, p.strips_per_row, b, wy, wx0);
+        const int64_t b = cur.b;
+        const int wy = cur.wy, wx0 = cur.wx0();
         uint8_t* st = smem + s * Lay::kStageBytes;
         mbar_arrive_expect_tx(&full[s], tx);
         tma_load_4d(st, &p.tm_h, &full[s], static_cast<int32_t>(c0), 4 * wx0, 4 * wy, static_cast<int32_t>(b), pol);
@@ -162,21 +195,21 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
   const bool cvalid = c < p.C;
   const uint32_t smem_base = smem_u32(smem);
 
-  if (WGRAD && warp < kWgradWarps) {
-    // ---------------- weight-gradient consumers (warp = cell row) ------------------
-    const int row = warp;
-    float2 acc[LMAX][4];
+  if (WGRAD && warp < Lay::kWgradWarps) {
+    // ---------------- weight-gradient consumers (cell row x layer group) ------------
+    constexpr int LW = Lay::kWgradLayers;
+    const int row = warp & 3;
+    const int l0 = (warp >> 2) * LW;
+    float2 acc[LW][4];
 #pragma unroll
-    for (int l = 0; l < LMAX; ++l)
+    for (int j = 0; j < LW; ++j)
 #pragma unroll
-      for (int col = 0; col < 4; ++col) acc[l][col] = make_float2(0.f, 0.f);
-    for (int it = 0; it < n_it; ++it) {
+      for (int col = 0; col < 4; ++col) acc[j][col] = make_float2(0.f, 0.f);
+    StripCursor cur(s_begin, p.G, p.strips_per_row);
+    for (int it = 0; it < n_it; ++it, cur.next()) {
       const int s = it % Lay::kStages;
       if (!mbar_wait(&full[s], (it / Lay::kStages) & 1)) break;
-      int64_t b;
-      int wy, wx0;
-      strip_coords(s_begin + it, p.G, p.strips_per_row, b, wy, wx0);
-      const int ncell = min(kStripCells, p.G - wx0);
+      const int ncell = min(kStripCells, p.G - cur.wx0());
       const uint32_t sb = smem_base + s * Lay::kStageBytes;
 #pragma unroll
       for (int k = 0; k < kStripCells; ++k) {
@@ -184,13 +217,14 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
           float2 h[4];
 #pragma unroll
           for (int col = 0; col < 4; ++col)
-            h[col] = lds_pair<T>(sb + ((row * 16 + 4 * k + col) * kSliceCh + 2 * lane) * kEs);
+            h[col] = lds_pair<T>(sb + ((row * kBoxCols + 4 * k + col) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-          for (int l = 0; l < LMAX; ++l) {
-            if (l < L) {
-              const float2 d = lds_pair<T>(sb + Lay::kHBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
+          for (int j = 0; j < LW; ++j) {
+            if (l0 + j < L) {
+              const float2 d =
+                  lds_pair<T>(sb + Lay::kHBytes + (((l0 + j) * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-              for (int col = 0; col < 4; ++col) acc[l][col] = ffma2(h[col], d, acc[l][col]);
+              for (int col = 0; col < 4; ++col) acc[j][col] = ffma2(h[col], d, acc[j][col]);
             }
           }
         }
@@ -201,12 +235,13 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
     if (cvalid) {
       float* P = p.partial + static_cast<int64_t>(blockIdx.x) * L * p.C * kPos;
 #pragma unroll
-      for (int l = 0; l < LMAX; ++l) {
+      for (int j = 0; j < LW; ++j) {
+        const int l = l0 + j;
         if (l < L) {
           *reinterpret_cast<float4*>(P + (l * p.C + c) * kPos + row * 4) =
-              make_float4(acc[l][0].x, acc[l][1].x, acc[l][2].x, acc[l][3].x);
+              make_float4(acc[j][0].x, acc[j][1].x, acc[j][2].x, acc[j][3].x);
           *reinterpret_cast<float4*>(P + (l * p.C + c + 1) * kPos + row * 4) =
-              make_float4(acc[l][0].y, acc[l][1].y, acc[l][2].y, acc[l][3].y);
+              make_float4(acc[j][0].y, acc[j][1].y, acc[j][2].y, acc[j][3].y);
         }
       }
     }
@@ -214,36 +249,41 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
   }
 
   if constexpr (POOL) {
-    // ---------------- pooling consumers (CELLS_PER_POOL cells each) ----------------
-    const int k0 = (warp - kPoolWarp0) * CELLS_PER_POOL;
+    // ---------------- pooling consumers (CELLS_PER_POOL cells x one layer group) ----
+    constexpr int GP = Lay::kGroupPairs;
+    const int pw = warp - kPoolWarp0;
+    const int k0 = (pw / Lay::kLayerGroups) * CELLS_PER_POOL;
+    const int lp0 = (pw % Lay::kLayerGroups) * GP;  // first layer pair of this warp
     const uint32_t wbase = smem_base + Lay::kWOffset + lane * 16;
     const int64_t GG = static_cast<int64_t>(p.G) * p.G;
-    for (int it = 0; it < n_it; ++it) {
+    StripCursor cur(s_begin, p.G, p.strips_per_row);
+    for (int it = 0; it < n_it; ++it, cur.next()) {
       const int s = it % Lay::kStages;
       if (!mbar_wait(&full[s], (it / Lay::kStages) & 1)) break;
-      int64_t b;
-      int wy, wx0;
-      strip_coords(s_begin + it, p.G, p.strips_per_row, b, wy, wx0);
+      const int64_t b = cur.b;
+      const int wy = cur.wy, wx0 = cur.wx0();
       const int ncell = min(kStripCells, p.G - wx0);
       const uint32_t sb = smem_base + s * Lay::kStageBytes;
-      float2 acc[LMAX][CELLS_PER_POOL];
+      float2 acc[2 * GP][CELLS_PER_POOL];
 #pragma unroll
-      for (int l = 0; l < LMAX; ++l)
+      for (int l = 0; l < 2 * GP; ++l)
 #pragma unroll
         for (int k = 0; k < CELLS_PER_POOL; ++k) acc[l][k] = make_float2(0.f, 0.f);
-#pragma unroll 2
+#pragma unroll kPoolUnroll
       for (int r = 0; r < kPos; ++r) {
         float2 h[CELLS_PER_POOL];
 #pragma unroll
         for (int k = 0; k < CELLS_PER_POOL; ++k)
-          h[k] = lds_pair<T>(sb + (((r >> 2) * 16 + 4 * (k0 + k) + (r & 3)) * kSliceCh + 2 * lane) * kEs);
+          h[k] = lds_pair<T>(sb + (((r >> 2) * kBoxCols + 4 * (k0 + k) + (r & 3)) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-        for (int lp = 0; lp < Lay::kLayerPairs; ++lp) {
-          const float4 wv = lds128f(wbase + (r * Lay::kLayerPairs + lp) * 32 * 16);
+        for (int j = 0; j < GP; ++j) {
+          if (lp0 + j < Lay::kLayerPairs) {
+            const float4 wv = lds128f(wbase + (r * Lay::kLayerPairs + lp0 + j) * 32 * 16);
 #pragma unroll
-          for (int k = 0; k < CELLS_PER_POOL; ++k) {
-            acc[2 * lp][k] = ffma2(make_float2(wv.x, wv.y), h[k], acc[2 * lp][k]);
-            if (2 * lp + 1 < LMAX) acc[2 * lp + 1][k] = ffma2(make_float2(wv.z, wv.w), h[k], acc[2 * lp + 1][k]);
+            for (int k = 0; k < CELLS_PER_POOL; ++k) {
+              acc[2 * j][k] = ffma2(make_float2(wv.x, wv.y), h[k], acc[2 * j][k]);
+              acc[2 * j + 1][k] = ffma2(make_float2(wv.z, wv.w), h[k], acc[2 * j + 1][k]);
+            }
           }
         }
       }
@@ -255,8 +295,10 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
         for (int k = 0; k < CELLS_PER_POOL; ++k) {
           if (k0 + k < ncell) {
 #pragma unroll
-            for (int l = 0; l < LMAX; ++l)
-              if (l < L) Act<T>::st(static_cast<T*>(p.out[l]) + (m0 + k0 + k) * p.C + c, acc[l][k]);
+            for (int j = 0; j < 2 * GP; ++j) {
+              const int l = 2 * lp0 + j;
+              if (l < L) Act<T>::st(static_cast<T*>(p.out[l]) + (m0 + k0 + k) * p.C + c, acc[j][k]);
+            }
           }
         }
       }
