@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_read_fwd": (_I, [_P, _P, _I, _P, _L, _L, _L, _I, _P]),
     "lthc_weight_grad_workspace_bytes": (c_size_t, [_L, _L, _L, _I]),
     "lthc_weight_grad": (_I, [_P, _PP, _I, _P, _P, c_size_t, _L, _L, _L, _I, _P]),
+    "lthc_weight_grad_noalloc": (_I, [_P, _PP, _I, _P, _L, _L, _L, _I, _P]),
     "lthc_read_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
     "lthc_read_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, c_size_t, _L, _L, _L, _I, _P]),
     "lthc_lazy_update_fwd": (_I, [_P, _P, _P, _I, _P, _I, _P, _L, _L, _I, _P]),

@@ -569,6 +569,59 @@ int lthc_weight_grad(const void* high, const void* const* low, int n_layers, flo
   return read_family(j, workspace_bytes, act_dtype, static_cast<cudaStream_t>(stream));
 }
 
+// ---- weight gradient without caller scratch -------------------------------------
+// The per-CTA partials of lthc_weight_grad_noalloc live in this fixed buffer, so
+// the call needs no workspace and allocates nothing.  Host code cannot use the
+// symbol itself as a device pointer: its device address is looked up once per
+// device with cudaGetSymbolAddress (with that device current) and cached.
+static __device__ __align__(256) float g_noalloc_scratch[LTHC_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[lthc::kMaxDevices] = {};
+
+static int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= lthc::kMaxDevices) {
+    cudaGetLastError();
+    return fail(LTHC_ERR_DEVICE, "no current CUDA device");
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return fail(LTHC_ERR_DEVICE, "cudaGetSymbolAddress of the internal scratch buffer failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return LTHC_OK;
+}
+
+int lthc_weight_grad_noalloc(const void* high, const void* const* low, int n_layers, float* grad_w, int64_t B,
+                             int64_t G, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_geometry(B, G, C, act_dtype));
+  LTHC_TRY(check_layers(n_layers));
+  LTHC_TRY(check_act(high, "high", B > 0));
+  LTHC_TRY(check_ptr(grad_w, "grad_w"));
+  if (!low) return fail(LTHC_ERR_NULL_POINTER, "low pointer array is NULL");
+  for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(low[l], "low[l]", B > 0));
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  const size_t need = wgrad_ws_bytes(B, G, C, n_layers, sms);
+  if (need > LTHC_NOALLOC_SCRATCH_BYTES)
+    return fail(LTHC_ERR_WORKSPACE,
+                "lthc_weight_grad_noalloc: this shape needs %zu bytes of partial sums, more than the fixed %u-byte "
+                "device buffer; call lthc_weight_grad with a caller-provided workspace instead",
+                need, LTHC_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if (B > 0) LTHC_TRY(noalloc_scratch(&ws));
+  ReadJob j{high, nullptr, LTHC_DTYPE_F32, nullptr, low, grad_w, ws, n_layers, B, G, C};
+  return read_family(j, LTHC_NOALLOC_SCRATCH_BYTES, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
 size_t lthc_read_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
   return lthc_materialise_bwd_workspace_bytes(B, G, C, 1);
 }

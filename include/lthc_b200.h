@@ -149,6 +149,30 @@ LTHC_API int lthc_weight_grad(const void* high, const void* const* low, int n_la
                      void* workspace, size_t workspace_bytes, int64_t B, int64_t G,
                      int64_t C, int act_dtype, void* stream);
 
+/* Size of the fixed device buffer behind lthc_weight_grad_noalloc (per GPU). */
+#define LTHC_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+
+/* Same result as lthc_weight_grad, but the caller passes no workspace and the
+ * library allocates nothing: the per-CTA partial sums live in a fixed
+ * LTHC_NOALLOC_SCRATCH_BYTES buffer compiled into the library (every GPU that
+ * loads the library holds it until the process exits).  No counterpart in the
+ * reference; it exists for callers that cannot allocate device memory at the
+ * call site: hosts that give an operator only its input and output buffers and
+ * own all other device memory, and callers that must not call cudaMalloc on
+ * that path because it can synchronise the device and stall other streams.
+ * Limits and behaviour:
+ *  - shapes whose partials do not fit the buffer (it grows with L, C and the
+ *    SM count; at C = 768 on 148 SMs it fits L <= 3) are rejected with
+ *    LTHC_ERR_WORKSPACE before anything is enqueued;
+ *  - the first call on each device looks up the buffer's device address
+ *    (a one-time set-up); make that first call before any stream capture;
+ *  - all calls on a device share the buffer: calls that may overlap on the GPU
+ *    (different streams, or threads without ordering) race and must be
+ *    serialised.  Each call writes every partial it later reads, so nothing is
+ *    carried over from the previous call. */
+LTHC_API int lthc_weight_grad_noalloc(const void* high, const void* const* low, int n_layers, float* grad_w,
+                                      int64_t B, int64_t G, int64_t C, int act_dtype, void* stream);
+
 /* Backward of the read:
  *   grad_x = (grad_x_in +) alpha (.) grad_z broadcast over each cell
  *   grad_alpha[c,r] = sum_{b,cell} x[b,cell,r,c] * grad_z[b,cell,c]   (fp32)
