@@ -45,7 +45,7 @@ TRAFFIC_FILE = ROOT / "profiles" / "materialise_fwd_b64_bf16.md"
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=B_DEFAULT, help="images per GPU (BASELINE config 2: 64)")

@@ -25,12 +25,16 @@ namespace lthc {
 
 // Pipeline shape.  A strip is kStripCells horizontally adjacent cells (its
 // residual box spans 4 * kStripCells token columns); 16-bit activations use
-// LTHC_STAGES_16BIT shared-memory stages per CTA, fp32 half as many.
+// LTHC_BCAST_STAGES_16BIT (write family) / LTHC_STAGES_16BIT (read family)
+// shared-memory stages per CTA, fp32 half as many.
 #ifndef LTHC_STRIP_CELLS
 #define LTHC_STRIP_CELLS 4
 #endif
 #ifndef LTHC_STAGES_16BIT
-#define LTHC_STAGES_16BIT 4
+#define LTHC_STAGES_16BIT 3   // read family (lthc_pool_tma.cuh)
+#endif
+#ifndef LTHC_BCAST_STAGES_16BIT
+#define LTHC_BCAST_STAGES_16BIT 6   // write family (this file)
 #endif
 constexpr int kStripCells = LTHC_STRIP_CELLS;
 constexpr int kBoxCols = 4 * kStripCells;
@@ -42,7 +46,7 @@ struct BcastLayout {
   static constexpr int kBaseBytes = 4 * kBoxCols * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kDzTileBytes = kStripCells * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kStageBytes = kBaseBytes + LMAX * kDzTileBytes;
-  static constexpr int kStages = sizeof(T) == 2 ? LTHC_STAGES_16BIT : (LTHC_STAGES_16BIT + 1) / 2;
+  static constexpr int kStages = sizeof(T) == 2 ? LTHC_BCAST_STAGES_16BIT : (LTHC_BCAST_STAGES_16BIT + 1) / 2;
   static constexpr int kBarrierOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarrierOffset + 2 * kStages * 8 + 128;  // + alignment slack
 };
