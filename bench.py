@@ -140,11 +140,21 @@ def time_device(fn, iters: int, stream: torch.cuda.Stream) -> float:
     return start.elapsed_time(end) / iters
 
 
+def host_threads() -> int:
+    """All host threads this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    so the CPU legs set their thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(seconds: float) -> dict:
     """The oracle (CPU restatement of the reference's algorithm) on a bounded
     sample of the same workload, all host threads."""
     from oracle import lthc_oracle as O
 
+    O.set_num_threads(host_threads())
     Bs = 4
     cfg = W.config2(B=Bs, seed=0)
     O.materialise(cfg["x0"], cfg["dz"], cfg["P"])
@@ -204,6 +214,7 @@ def reference_arm(args, r: D.Rank) -> int:
         return 0
     from oracle import lthc_oracle as O
 
+    O.set_num_threads(host_threads())
     per_step_s = 0.035  # measured B=4 cost of the oracle materialisation on 8 cores
     Bs = 4 if (args.steps + args.warmup) * per_step_s <= 120 else 1
     cfg = W.config2(B=Bs, seed=0)
@@ -264,7 +275,7 @@ def main() -> int:
         return 1
     torch.cuda.set_device(r.local_rank)
     dev = torch.device("cuda", r.local_rank)
-    D.init("nccl", r)
+    D.init("nccl", r, device=dev)
     stream = torch.cuda.current_stream(dev)
     B = args.batch
 

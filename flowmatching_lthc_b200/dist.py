@@ -31,11 +31,13 @@ def from_env() -> Rank:
                 int(os.environ.get("LOCAL_RANK", "0")))
 
 
-def init(backend: str, r: Rank, timeout_s: float = 120.0) -> None:
-    """Initialise the default process group (no-op for a single rank)."""
+def init(backend: str, r: Rank, timeout_s: float = 120.0, device: torch.device | None = None) -> None:
+    """Initialise the default process group (no-op for a single rank).  `device`
+    binds an NCCL group to this rank's GPU."""
     if r.world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group(backend, rank=r.rank, world_size=r.world, timeout=timedelta(seconds=timeout_s))
+        kw = {"device_id": device} if device is not None else {}
+        dist.init_process_group(backend, rank=r.rank, world_size=r.world, timeout=timedelta(seconds=timeout_s), **kw)
 
 
 def shard(total: int, rank: int, world: int) -> tuple[int, int]:
