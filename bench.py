@@ -51,7 +51,7 @@ def parse_args():
     p.add_argument("--batch", type=int, default=B_DEFAULT, help="images per GPU (BASELINE config 2: 64)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     p.add_argument("--no-extras", action="store_true", help="skip the per-kernel and comparator measurements")
-    p.add_argument("--op", default="materialise_fwd", choices=sorted(OPS),
+    p.add_argument("--op", default="materialise_fwd", choices=sorted(OPS + MODEL_OPS),
                    help="the LTHC op timed as the step (default: the BASELINE config 2 materialisation)")
     return p.parse_args()
 
@@ -206,6 +206,140 @@ def op_step(op: str, cfg: dict):
 
 
 OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd")
+MODEL_OPS = ("model_fwd", "train_step", "sample")
+# Largest batch per model call for which the reference Triton materialisation's
+# 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
+REF_TRITON_MAX_BATCH = (2**31 - 1) // (4096 * 768)
+
+
+# ------------------------------------------------------------------ model-level workloads
+def _reference_model(dev):
+    """The released LTHC-B/4 model from the reference package (baseline/_ref), random
+    init with its zero-initialised layers (AdaLN, final linear) re-seeded so that the
+    output is not identically zero."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "flowmatching_lthc").exists():
+        raise RuntimeError("model-level workloads need the reference package under baseline/_ref")
+    sys.path.insert(0, str(ref))
+    import flowmatching_lthc.models.local_thc as Lm
+    from flowmatching_lthc.models import build_model
+
+    torch.manual_seed(0)
+    m = build_model("lthc_b4_velocity").to(dev)
+    g = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        for name, prm in m.named_parameters():
+            if name.endswith("read_logits"):
+                prm.copy_(torch.randn(prm.shape, generator=g))
+            elif name.endswith("write_weight"):
+                prm.copy_(1.0 + 0.1 * torch.randn(prm.shape, generator=g))
+            elif torch.count_nonzero(prm) == 0:
+                prm.copy_(0.02 * torch.randn(prm.shape, generator=g))
+    return m, Lm
+
+
+def model_bench(args, r: D.Rank, dev, stream) -> dict:
+    """Images/sec of the reference model with the LTHC interface on the new kernels
+    (integration.install) and with the reference's own GPU path (eager + Triton),
+    same process, same inputs.  model_fwd = BASELINE config 3 (B=64 bf16 forward);
+    train_step = config 4 (32 images per GPU, fwd + bwd + fused AdamW, DDP for N>1);
+    sample = config 5 (Heun-50, CFG 1.5, 1024 images sharded over the GPUs; ours
+    uses the doubled-batch sampler, the reference its two-call sampler)."""
+    from flowmatching_lthc_b200 import integration
+    from flowmatching_lthc_b200.sampling import sample_heun as sample_doubled
+
+    m, Lm = _reference_model(dev)
+    gen = torch.Generator(device=dev).manual_seed(2000 + r.rank)
+    op = args.op
+    if op == "model_fwd":
+        B = args.batch
+        m.eval()
+        x = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+        t = torch.rand(B, device=dev, generator=gen)
+        y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
+
+        def step():
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                m(x, t, y)
+        per_step, warm, steps = B, max(args.warmup, 3), args.steps
+    elif op == "train_step":
+        B = 32
+        m.train()
+        net = m
+        if r.world > 1:
+            net = torch.nn.parallel.DistributedDataParallel(m, device_ids=[r.local_rank])
+        opt = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True)
+        x1 = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+        x0 = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+        t = torch.rand(B, device=dev, generator=gen)
+        y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
+        tt = t.view(-1, 1, 1, 1)
+        z = tt * x1 + (1 - tt) * x0
+        v = (x1 - z) / (1 - tt).clamp_min(0.05)
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = (v - net(z, t, y)).float().square().mean()
+            loss.backward()
+            opt.step()
+        per_step, warm, steps = B, max(args.warmup, 3), args.steps
+    else:  # sample
+        n_img = D.shard(1024, r.rank, r.world)
+        nb = n_img[1] - n_img[0]
+        m.eval()
+        labels = torch.randint(0, 1000, (1024,), generator=torch.Generator().manual_seed(5))[n_img[0]:n_img[1]].to(dev)
+        noise = torch.randn(1024, 3, 256, 256, generator=torch.Generator().manual_seed(6))[n_img[0]:n_img[1]].to(dev)
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        from flowmatching_lthc.sampling import sample_heun as sample_ref
+        state = {"installed": True}
+
+        def step(n_steps=50):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                if state["installed"]:
+                    sample_doubled(m, labels, steps=n_steps, cfg_scale=1.5, noise=noise, prediction="velocity")
+                else:
+                    torch.manual_seed(6)
+                    sample_ref(m, labels, steps=n_steps, cfg_scale=1.5, prediction="velocity")
+        per_step, warm, steps = nb, 1, max(1, min(args.steps, 2))
+
+    def timed(installed: bool) -> float:
+        handle = integration.install(Lm) if installed else None
+        if op == "sample":
+            state["installed"] = installed
+            step(2)  # warm-up: compiles the reference's Triton op, fills the allocator
+        else:
+            for _ in range(warm):
+                step()
+        torch.cuda.synchronize()
+        D.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+        D.barrier()
+        if handle:
+            handle.uninstall()
+        return D.reduce_max(e0.elapsed_time(e1), dev)
+
+    ms_ours = timed(True)
+    total = (1024 if op == "sample" else per_step * r.world) * steps
+    out = {"ms_ours": ms_ours, "images": total, "steps": steps, "value": total / (ms_ours / 1e3)}
+    # The reference's fused materialisation (Triton, local_thc_triton_kernels.py:317-405)
+    # computes element offsets in 32-bit integers; at the B/4 shape they wrap for a
+    # model call with more than REF_TRITON_MAX_BATCH images, and running it there
+    # raised an illegal memory access on this pool.  Its GPU path is not run there.
+    ref_batch = per_step  # images per model call in the reference arm
+    if ref_batch > REF_TRITON_MAX_BATCH:
+        out["ref_unavailable"] = (f"reference Triton materialise op overflows 32-bit offsets for more than "
+                                  f"{REF_TRITON_MAX_BATCH} images per call (this call: {ref_batch}); not run")
+    else:
+        ms_ref = timed(False)
+        out.update(ms_ref=ms_ref, ref_value=total / (ms_ref / 1e3))
+    return out
+
 
 
 # ------------------------------------------------------------------ reference arm
@@ -278,6 +412,31 @@ def main() -> int:
     D.init("nccl", r, device=dev)
     stream = torch.cuda.current_stream(dev)
     B = args.batch
+
+    if args.op in MODEL_OPS:
+        res = model_bench(args, r, dev, stream)
+        if r.is_main:
+            cfg_model = {"workload": {"model_fwd": "LTHC-B/4 random-init forward, BASELINE config 3",
+                                      "train_step": "LTHC-B/4 velocity training step fwd+bwd+AdamW, BASELINE config 4",
+                                      "sample": "Heun-50 CFG 1.5 sampling of 1024 images, BASELINE config 5"}[args.op],
+                         "op": args.op, "model": "lthc_b4_velocity (reference code, random init)",
+                         "batch_per_gpu": {"model_fwd": B, "train_step": 32}.get(args.op, 1024 // r.world),
+                         "image_size": 256, "dtype": "bf16 autocast", "parallelism": f"dp{r.world}"}
+            print(json.dumps({
+                "metric": "LTHC-B/4 images/sec", "value": round(res["value"], 2), "unit": "images/s",
+                "n_gpus": r.world, "steps": res["steps"], "warmup": args.warmup,
+                "ms_per_step": round(res["ms_ours"] / res["steps"], 3), "higher_is_better": True,
+                "scaling": "strong" if args.op == "sample" else "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic images/noise/labels, random-init weights", "config": cfg_model,
+                "reference_gpu": ({"value": round(res["ref_value"], 2), "unit": "images/s",
+                                   "ms_per_step": round(res["ms_ref"] / res["steps"], 3),
+                                   "path": "reference eager LTHC + Triton materialise (uninstalled)"}
+                                  if "ref_value" in res else {"unavailable": res["ref_unavailable"]}),
+                "speedup_vs_reference_gpu": (round(res["value"] / res["ref_value"], 4) if "ref_value" in res
+                                             else None)}), flush=True)
+        D.barrier()
+        D.shutdown()
+        return 0
 
     cfg = _op_inputs(B, dev, seed=1000 + r.rank)
     step, bytes_step, launches, kernel = op_step(args.op, cfg)

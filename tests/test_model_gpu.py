@@ -121,3 +121,26 @@ def test_triton_materialise_comparator_parity():
     except Exception as e:
         pytest.skip(f"reference Triton op unavailable here: {type(e).__name__}: {e}")
     assert rel_err(ours, theirs) < 2e-2
+
+
+def test_doubled_batch_sampler_matches_the_reference_sampler():
+    """sample_heun with one [cond; uncond] forward per step gives the reference's
+    two-call CFG Heun result (same noise), with and without the new kernels."""
+    L = import_reference()
+    from flowmatching_lthc.sampling import sample_heun as reference_sample
+
+    from flowmatching_lthc_b200.sampling import sample_heun
+
+    m = small_model(L).eval()
+    labels = torch.tensor([1, 5, 999], device="cuda")
+    kw = dict(image_size=64, steps=4, cfg_scale=1.5, interval=(0.1, 1.0), prediction="velocity")
+    torch.manual_seed(3)
+    ref = reference_sample(m, labels, **kw)
+    torch.manual_seed(3)
+    ours = sample_heun(m, labels, **kw)
+    assert ref.abs().max() > 0
+    assert rel_err(ours, ref) < 1e-4
+    with integration.install(L):
+        torch.manual_seed(3)
+        ours_kernels = sample_heun(m, labels, **kw)
+    assert rel_err(ours_kernels, ref) < 1e-4

@@ -275,6 +275,24 @@ def test_materialise_config2_full_size():
 
 
 @pytest.mark.slow
+def test_materialise_and_read_beyond_2pow31_elements():
+    """B = 700 at the B/4 shape: the residual has 2.2e9 elements, more than a 32-bit
+    offset can address (the reference's Triton materialisation wraps there).  The
+    first and last images must match the oracle bit for bit."""
+    B = 700
+    cfg = workloads.config2(B=B, device="cuda", seed=9)
+    x0, dz, P = cfg["x0"], cfg["dz"], cfg["P"]
+    assert x0.numel() > 2**31
+    out = F.materialise(x0, dz, P)
+    alpha = torch.softmax(cfg["R"], -1)
+    z = F.read(out, alpha)
+    for b in (0, B - 1):
+        ref = O.materialise(x0[b:b + 1].cpu(), [d[b:b + 1].cpu() for d in dz], [p.cpu() for p in P])
+        assert same_bits(out[b:b + 1], ref)
+        assert same_bits(z[b:b + 1], O.read(ref, alpha.cpu()))
+
+
+@pytest.mark.slow
 def test_lazy_identity_full_size_fp32():
     """read(X_0 + sum_l P_l dZ_l) == read(X_0) + sum_l Gamma_l dZ_l at the B/4 geometry."""
     cfg = workloads.config2(B=8, device="cuda", seed=1, dtype=torch.float32)
