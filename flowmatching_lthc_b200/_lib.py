@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_status_string": (c_char_p, [_I]),
     "lthc_last_error_message": (c_char_p, []),
     "lthc_device_status": (_I, [POINTER(c_int), _P]),
+    "lthc_selftest_wait_timeout": (_I, [_I, _P, _P]),
     "lthc_write_fwd": (_I, [_P, _P, _I, _P, _L, _L, _L, _I, _P]),
     "lthc_write_add_fwd": (_I, [_P, _P, _P, _I, _P, _L, _L, _L, _I, _P]),
     "lthc_materialise_fwd": (_I, [_P, _PP, _PP, _I, _I, _P, _L, _L, _L, _I, _P]),

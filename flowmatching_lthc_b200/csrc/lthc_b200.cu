@@ -443,6 +443,16 @@ int lthc_device_status(int* status_out, void* stream) {
   return LTHC_OK;
 }
 
+int lthc_selftest_wait_timeout(int limit_ms, int* result_dev, void* stream) {
+  if (limit_ms < 1 || limit_ms > 5000) return fail(LTHC_ERR_SHAPE, "limit_ms must be in [1, 5000], got %d", limit_ms);
+  LTHC_TRY(check_ptr(result_dev, "result_dev"));
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(limit_ms) * 1000000ull, result_dev);
+  return launched("wait-timeout self-test");
+}
+
 // ------------------------------ write family ---------------------------------
 
 int lthc_write_fwd(const void* dz, const void* beta, int beta_dtype, void* out, int64_t B, int64_t G, int64_t C,

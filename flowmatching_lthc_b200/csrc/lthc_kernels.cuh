@@ -97,6 +97,11 @@ __device__ __forceinline__ void st_vec(T* p, const float (&v)[Vec16<T>::V]) {
   *reinterpret_cast<uint4*>(p) = raw;
 }
 
+// Rows handled per batch by one lane: all their loads are issued before any
+// store, so a lane keeps 2 * kLazyBatch 16-byte loads in flight even though the
+// output may alias an input (in-place update).
+constexpr int kLazyBatch = 4;
+
 template <typename T>
 __global__ void __launch_bounds__(256) lazy_fwd_kernel(const __grid_constant__ LazyParams p) {
   constexpr int V = Vec16<T>::V;
@@ -113,20 +118,31 @@ __global__ void __launch_bounds__(256) lazy_fwd_kernel(const __grid_constant__ L
   const T* z = static_cast<const T*>(p.z);
   const T* dz = static_cast<const T*>(p.dz);
   T* out = static_cast<T*>(p.out);
-#pragma unroll 4
-  for (int64_t n = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n < p.N;
-       n += static_cast<int64_t>(gridDim.x) * kLazyWarps) {
-    const int64_t off = n * p.C + c;
-    float zv[V], dv[V];
-    ld_vec<T>(z + off, zv);
-    ld_vec<T>(dz + off, dv);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kLazyWarps;
+  for (int64_t n0 = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n0 < p.N; n0 += stride * kLazyBatch) {
+    float zv[kLazyBatch][V], dv[kLazyBatch][V];
 #pragma unroll
-    for (int i = 0; i < V; i += 2) {
-      const float2 r = ffma2(make_float2(g[i], g[i + 1]), make_float2(dv[i], dv[i + 1]), make_float2(zv[i], zv[i + 1]));
-      zv[i] = r.x;
-      zv[i + 1] = r.y;
+    for (int j = 0; j < kLazyBatch; ++j) {
+      const int64_t n = n0 + j * stride;
+      if (n < p.N) {
+        ld_vec<T>(z + n * p.C + c, zv[j]);
+        ld_vec<T>(dz + n * p.C + c, dv[j]);
+      }
     }
-    st_vec<T>(out + off, zv);
+#pragma unroll
+    for (int j = 0; j < kLazyBatch; ++j) {
+      const int64_t n = n0 + j * stride;
+      if (n < p.N) {
+#pragma unroll
+        for (int i = 0; i < V; i += 2) {
+          const float2 r = ffma2(make_float2(g[i], g[i + 1]), make_float2(dv[j][i], dv[j][i + 1]),
+                                 make_float2(zv[j][i], zv[j][i + 1]));
+          zv[j][i] = r.x;
+          zv[j][i + 1] = r.y;
+        }
+        st_vec<T>(out + n * p.C + c, zv[j]);
+      }
+    }
   }
 }
 
@@ -151,24 +167,35 @@ __global__ void __launch_bounds__(256) lazy_bwd_kernel(const __grid_constant__ L
     const T* gz = static_cast<const T*>(p.z);
     const T* dz = static_cast<const T*>(p.dz);
     T* gdz = static_cast<T*>(p.out);
-#pragma unroll 4
-    for (int64_t n = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n < p.N;
-         n += static_cast<int64_t>(gridDim.x) * kLazyWarps) {
-      const int64_t off = n * p.C + c;
-      float gv[V], dv[V], o[V];
-      ld_vec<T>(gz + off, gv);
-      ld_vec<T>(dz + off, dv);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kLazyWarps;
+    for (int64_t n0 = static_cast<int64_t>(blockIdx.x) * kLazyWarps + warp; n0 < p.N; n0 += stride * kLazyBatch) {
+      float gv[kLazyBatch][V], dv[kLazyBatch][V];
 #pragma unroll
-      for (int i = 0; i < V; i += 2) {
-        const float2 m = fmul2(make_float2(g[i], g[i + 1]), make_float2(gv[i], gv[i + 1]));
-        o[i] = m.x;
-        o[i + 1] = m.y;
-        const float2 a2 = ffma2(make_float2(gv[i], gv[i + 1]), make_float2(dv[i], dv[i + 1]),
-                                make_float2(acc[i], acc[i + 1]));
-        acc[i] = a2.x;
-        acc[i + 1] = a2.y;
+      for (int j = 0; j < kLazyBatch; ++j) {
+        const int64_t n = n0 + j * stride;
+        if (n < p.N) {
+          ld_vec<T>(gz + n * p.C + c, gv[j]);
+          ld_vec<T>(dz + n * p.C + c, dv[j]);
+        }
       }
-      st_vec<T>(gdz + off, o);
+#pragma unroll
+      for (int j = 0; j < kLazyBatch; ++j) {
+        const int64_t n = n0 + j * stride;
+        if (n < p.N) {
+          float o[V];
+#pragma unroll
+          for (int i = 0; i < V; i += 2) {
+            const float2 m = fmul2(make_float2(g[i], g[i + 1]), make_float2(gv[j][i], gv[j][i + 1]));
+            o[i] = m.x;
+            o[i + 1] = m.y;
+            const float2 a2 = ffma2(make_float2(gv[j][i], gv[j][i + 1]), make_float2(dv[j][i], dv[j][i + 1]),
+                                    make_float2(acc[i], acc[i + 1]));
+            acc[i] = a2.x;
+            acc[i + 1] = a2.y;
+          }
+          st_vec<T>(gdz + n * p.C + c, o);
+        }
+      }
     }
   }
 #pragma unroll

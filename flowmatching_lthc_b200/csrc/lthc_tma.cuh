@@ -64,17 +64,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs, records the failure in g_device_error and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// limit_ns, records the failure in g_device_error and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((i & 255u) == 0 && global_timer_ns() - t0 > limit_ns) {
       atomicExch(&g_device_error, 1);
       return false;
     }
   }
+}
+
+// Diagnostic kernel: waits on an mbarrier that nothing will ever complete, with
+// the given limit, so that the timeout path (error word set, kernel returns,
+// context stays usable) can be exercised.  `out` receives 1 if the wait gave up.
+__global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns, int* out) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, limit_ns);  // phase 0 never completes: no arrival
+  if (threadIdx.x == 0) *out = ok ? 0 : 1;
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {

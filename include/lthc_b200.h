@@ -73,6 +73,14 @@ LTHC_API const char* lthc_last_error_message(void);
  * `stream`.  *status_out receives LTHC_OK or LTHC_ERR_TIMEOUT. */
 LTHC_API int lthc_device_status(int* status_out, void* stream);
 
+/* Diagnostic: enqueues a one-block kernel that waits on a barrier nothing will
+ * complete, giving up after limit_ms milliseconds (1..5000) the same way every
+ * kernel's bounded waits do: it sets the device error word (seen afterwards by
+ * lthc_device_status as LTHC_ERR_TIMEOUT), writes 1 to *result_dev (a device int)
+ * and returns, leaving the CUDA context usable.  No counterpart in the reference
+ * (whose failure handling is host-side only, scripts/evaluate_fid.py:333-351). */
+LTHC_API int lthc_selftest_wait_timeout(int limit_ms, int* result_dev, void* stream);
+
 /* ======================= write family: workspace -> residual ============== */
 
 /* out[b,cell,r,c] = beta[c,r] * dz[b,cell,c]

@@ -349,3 +349,22 @@ def test_cuda_graph_capture_replay():
     g.replay()
     torch.cuda.synchronize()
     assert same_bits(out, expect)
+
+
+# ------------------------------------------------------------------ failure detection
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """A wait on a barrier nothing completes gives up after its limit, the device
+    error word reports LTHC_ERR_TIMEOUT, and the next kernels run normally."""
+    res = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    _lib.call("lthc_selftest_wait_timeout", 50, res.data_ptr(), s)
+    st = ctypes.c_int(-1)
+    _lib.call("lthc_device_status", ctypes.byref(st), s)
+    assert st.value == 8 and int(res.item()) == 1
+    assert device_status_ok()  # reading cleared the word
+    B, G, C = 1, 4, 64
+    x0 = rnd(B, 4 * G, 4 * G, C, dtype=torch.bfloat16, seed=300)
+    dz = [rnd(B, G * G, C, dtype=torch.bfloat16, seed=301)]
+    beta = [rnd(C, 16, seed=302)]
+    out = F.materialise(x0.cuda(), [d.cuda() for d in dz], [b.cuda() for b in beta])
+    assert same_bits(out, O.materialise(x0, dz, beta))
