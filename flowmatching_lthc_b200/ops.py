@@ -14,6 +14,7 @@ can switch by changing its import.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from typing import Sequence
 
@@ -74,6 +75,15 @@ def _check_weight(w: Tensor, c: int, what: str) -> None:
         raise ValueError(f"{what}: expected weight [{c},16], got {tuple(w.shape)}")
 
 
+def _guard(t: Tensor):
+    """Make t's GPU current for the C call (the library launches on the current
+    device); a no-op context when it already is."""
+    idx = t.device.index
+    if idx is None or torch.cuda.current_device() == idx:
+        return contextlib.nullcontext()
+    return torch.cuda.device(idx)
+
+
 def _stream(t: Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
@@ -98,7 +108,7 @@ def read(x: Tensor, alpha: Tensor) -> Tensor:
     _check_weight(alpha, c, "read")
     x, alpha = x.contiguous(), alpha.contiguous()
     z = torch.empty((b, g * g, c), device=x.device, dtype=x.dtype)
-    with torch.cuda.device(x.device):
+    with _guard(x):
         _lib.call("lthc_read_fwd", x.data_ptr(), alpha.data_ptr(), _code(alpha, "read"), z.data_ptr(), b, g, c,
                   _code(x, "read"), _stream(x))
     return z
@@ -119,7 +129,7 @@ def read_bwd(x: Tensor, grad_z: Tensor, alpha: Tensor, need_grad_x: bool, need_g
     gx = torch.empty_like(x) if need_grad_x else x.new_empty((0,))
     ga = torch.empty((c, 16), device=x.device, dtype=torch.float32) if need_grad_alpha else x.new_empty((0,),
                                                                                                       dtype=torch.float32)
-    with torch.cuda.device(x.device):
+    with _guard(x):
         ws_bytes = _lib.load().lthc_read_bwd_workspace_bytes(b, g, c) if need_grad_alpha else 0
         ws = _workspace(ws_bytes, x.device) if need_grad_alpha else None
         _lib.call("lthc_read_bwd", x.data_ptr(), grad_z.data_ptr(), alpha.data_ptr(), _code(alpha, "read_bwd"), None,
@@ -177,7 +187,7 @@ def _materialise_impl(x0: Tensor | None, dz: Sequence[Tensor], beta: Sequence[Te
             raise ValueError(f"materialise: expected x0 [{b},{4 * g},{4 * g},{c}], got {tuple(x0.shape)}")
         x0 = x0.to(act).contiguous()
     out = torch.empty((b, 4 * g, 4 * g, c), device=dz[0].device, dtype=act)
-    with torch.cuda.device(out.device):
+    with _guard(out):
         _lib.call("lthc_materialise_fwd", _p(x0), _lib.ptr_array([t.data_ptr() for t in dz]),
                   _lib.ptr_array([w.data_ptr() for w in beta]), _code(beta[0], "materialise"), L, out.data_ptr(), b, g,
                   c, _code(out, "materialise"), _stream(out))
@@ -214,7 +224,7 @@ def materialise_bwd(grad_out: Tensor, dz: list[Tensor], beta: list[Tensor], need
     gdz = [torch.empty((b, g * g, c), device=grad_out.device, dtype=act) for _ in range(L)] if need_grad_dz else []
     gbeta = (torch.empty((L, c, 16), device=grad_out.device, dtype=torch.float32) if need_grad_beta
              else grad_out.new_empty((0,), dtype=torch.float32))
-    with torch.cuda.device(grad_out.device):
+    with _guard(grad_out):
         ws_bytes = _lib.load().lthc_materialise_bwd_workspace_bytes(b, g, c, L) if need_grad_beta else 0
         ws = _workspace(ws_bytes, grad_out.device) if need_grad_beta else None
         _lib.call("lthc_materialise_bwd", grad_out.data_ptr(), _lib.ptr_array([t.data_ptr() for t in dz]),
@@ -267,7 +277,7 @@ def write(dz: Tensor, beta: Tensor) -> Tensor:
     _check_weight(beta, c, "write")
     dz, beta = dz.contiguous(), beta.contiguous()
     out = torch.empty((b, 4 * g, 4 * g, c), device=dz.device, dtype=dz.dtype)
-    with torch.cuda.device(dz.device):
+    with _guard(dz):
         _lib.call("lthc_write_fwd", dz.data_ptr(), beta.data_ptr(), _code(beta, "write"), out.data_ptr(), b, g, c,
                   _code(dz, "write"), _stream(dz))
     return out
@@ -289,7 +299,7 @@ def write_bwd(grad_out: Tensor, dz: Tensor, beta: Tensor, need_grad_dz: bool, ne
     gdz = torch.empty((b, g * g, c), device=dz.device, dtype=grad_out.dtype) if need_grad_dz else dz.new_empty((0,))
     gb = (torch.empty((c, 16), device=dz.device, dtype=torch.float32) if need_grad_beta
           else dz.new_empty((0,), dtype=torch.float32))
-    with torch.cuda.device(dz.device):
+    with _guard(dz):
         ws_bytes = _lib.load().lthc_write_bwd_workspace_bytes(b, g, c) if need_grad_beta else 0
         ws = _workspace(ws_bytes, dz.device) if need_grad_beta else None
         _lib.call("lthc_write_bwd", grad_out.data_ptr(), dz.data_ptr(), beta.data_ptr(), _code(beta, "write_bwd"),
@@ -333,7 +343,7 @@ def write_add(x_hi: Tensor, dz: Tensor, beta: Tensor) -> Tensor:
     _check_weight(beta, c, "write_add")
     x_hi, dz, beta = x_hi.contiguous(), dz.to(x_hi.dtype).contiguous(), beta.contiguous()
     out = torch.empty_like(x_hi)
-    with torch.cuda.device(x_hi.device):
+    with _guard(x_hi):
         _lib.call("lthc_write_add_fwd", x_hi.data_ptr(), dz.data_ptr(), beta.data_ptr(), _code(beta, "write_add"),
                   out.data_ptr(), b, g, c, _code(x_hi, "write_add"), _stream(x_hi))
     return out
@@ -378,7 +388,7 @@ def lazy_update(z: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor) -> Tensor:
     z, dz, alpha, beta = z.contiguous(), dz.to(z.dtype).contiguous(), alpha.contiguous(), beta.contiguous()
     out = torch.empty_like(z)
     n = z.numel() // c
-    with torch.cuda.device(z.device):
+    with _guard(z):
         _lib.call("lthc_lazy_update_fwd", z.data_ptr(), dz.data_ptr(), alpha.data_ptr(), _code(alpha, "lazy_update"),
                   beta.data_ptr(), _code(beta, "lazy_update"), out.data_ptr(), n, c, _code(z, "lazy_update"),
                   _stream(z))
@@ -401,7 +411,7 @@ def lazy_update_bwd(grad_z_out: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor)
     gdz = torch.empty_like(g)
     ga = torch.empty((c, 16), device=g.device, dtype=torch.float32)
     gb = torch.empty((c, 16), device=g.device, dtype=torch.float32)
-    with torch.cuda.device(g.device):
+    with _guard(g):
         ws_bytes = _lib.load().lthc_lazy_update_bwd_workspace_bytes(n, c)
         ws = _workspace(ws_bytes, g.device)
         _lib.call("lthc_lazy_update_bwd", g.data_ptr(), dz.data_ptr(), alpha.data_ptr(),
@@ -451,7 +461,7 @@ def weight_grad(high: Tensor, low: list[Tensor]) -> Tensor:
         if tuple(t.shape) != (b, g * g, c):
             raise ValueError(f"weight_grad: expected low [{b},{g * g},{c}], got {tuple(t.shape)}")
     out = torch.empty((L, c, 16), device=high.device, dtype=torch.float32)
-    with torch.cuda.device(high.device):
+    with _guard(high):
         ws_bytes = _lib.load().lthc_weight_grad_workspace_bytes(b, g, c, L)
         ws = _workspace(ws_bytes, high.device)
         _lib.call("lthc_weight_grad", high.data_ptr(), _lib.ptr_array([t.data_ptr() for t in low]), L, out.data_ptr(),
