@@ -386,3 +386,38 @@ def test_materialise_from_host_buffers_pipelined():
         hm(x0.pin_memory(), [d.pin_memory() for d in dz], P, out)
         torch.cuda.synchronize()
         assert same_bits(out, O.materialise(x0, dz, [p.cpu() for p in P]))
+
+
+def test_torch_compile_fullgraph_forward_and_backward():
+    """The ops trace under torch.compile (fake implementations + registered autograd)
+    and the compiled graph gives the eager results bit for bit (weight gradients summed over
+    several uses: up to fp32 reassociation)."""
+    torch._dynamo.reset()
+    B, G, C, L = 2, 4, 64, 3
+    dt = torch.bfloat16
+    x0 = rnd(B, 4 * G, 4 * G, C, dtype=dt, seed=500).cuda()
+    dz = [rnd(B, G * G, C, dtype=dt, std=0.1, seed=501 + l).cuda() for l in range(L)]
+    P = [rnd(C, 16, std=0.02, mean=1.0, seed=510 + l).cuda() for l in range(L)]
+    # alpha enters as an fp32 leaf: a softmax or bf16 cast inside the graph would be
+    # fused by the compiler with its own rounding, which is not what this test checks.
+    alpha0 = torch.softmax(rnd(C, 16, seed=520), -1).cuda()
+
+    def f(x0, dz, P, alpha):
+        z = ops.read(x0, alpha)
+        for d, p in zip(dz, P):
+            z = ops.lazy_update(z, d, alpha, p)
+        xl = ops.materialise(x0, dz, P)
+        return (z.float().square().sum() + xl.float().square().sum()), z, xl
+
+    def run(fn):
+        a = [x0.clone().requires_grad_(True)] + [d.clone().requires_grad_(True) for d in dz]
+        ps = [p.clone().requires_grad_(True) for p in P]
+        lg = alpha0.clone().requires_grad_(True)
+        loss, z, xl = fn(a[0], a[1:], ps, lg)
+        loss.backward()
+        return [z, xl] + [t.grad for t in a + ps + [lg]]
+
+    eager = run(f)
+    compiled = run(torch.compile(f, fullgraph=True))
+    for e, c in zip(eager, compiled):
+        assert same_bits(c, e) or rel_err(c, e) < RTOL_REDUCTION
