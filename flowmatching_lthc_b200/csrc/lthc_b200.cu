@@ -257,15 +257,16 @@ int resident_ctas(Kernel kern, int threads, int smem_bytes, int* out) {
 // ---- dispatch helpers -----------------------------------------------------
 template <typename T, int LT, bool HB>
 int launch_broadcast_tma(BcastTmaParams& p, int sms, cudaStream_t s) {
-  using Lay = BcastLayout<T, (LT > 0 ? LT : kMaxLayers)>;
+  using Lay = BcastLayout<T, LT, HB>;
+  constexpr int kThreads = Lay::Shape::kThreads;
   auto kern = broadcast_tma_kernel<T, LT, HB>;
   int per_sm = 1;
-  LTHC_TRY(resident_ctas(kern, kBcastThreads, Lay::kSmemBytes, &per_sm));
+  LTHC_TRY(resident_ctas(kern, kThreads, Lay::kSmemBytes, &per_sm));
   const int64_t slices = slices_of(p.C);
   int64_t nx = one_wave_columns(p.strips, p.C, sms, per_sm);
   p.strips_per_cta = ceil_div(p.strips, nx);
   nx = ceil_div(p.strips, p.strips_per_cta);
-  kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), kBcastThreads, Lay::kSmemBytes, s>>>(p);
+  kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), kThreads, Lay::kSmemBytes, s>>>(p);
   return launched("broadcast (TMA)");
 }
 

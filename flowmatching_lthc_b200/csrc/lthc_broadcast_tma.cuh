@@ -2,14 +2,15 @@
 // over each 4x4 cell (write, write_add, the fused materialisation and the read
 // backward's grad_x).
 //
-// CTA = 4 consumer warps + 1 producer warp, owning one 64-channel slice of the
+// CTA = consumer warps + 1 producer warp, owning one 64-channel slice of the
 // residual.  The producer's elected lane streams "strips" of kStripCells
 // horizontally adjacent cells into a ring of shared-memory stages with TMA:
 //   base tile  [4 rows][4*strip columns][64 channels] (box of the NHWC residual)
 //   dz tiles   [L][4 cells][64 channels]           (box of each workspace update)
-// Consumer warp `row` owns cell row `row`; lane l owns channel pair (2l, 2l+1)
-// and keeps w_l[c, 4*row + col] for all L layers and 4 columns in registers, so
-// each weight is loaded once per CTA.  Per cell a lane reads 4 base pairs and
+// A consumer warp owns one cell row (or, for L = 1 with a base, one position of
+// the row: BcastShape); lane l owns channel pair (2l, 2l+1) and keeps
+// w_l[c, 4*row + col] for all L layers and its columns in registers, so each
+// weight is loaded once per CTA.  Per cell a lane reads 4 base pairs and
 // L update pairs from shared memory (128 contiguous bytes per warp access, no
 // bank conflicts), accumulates in fp32 with packed fp32x2 FMAs in the order
 // base, l = 0, 1, ... and writes the rounded result back over the base tile,
@@ -34,21 +35,67 @@ namespace lthc {
 #define LTHC_STAGES_16BIT 3   // read family (lthc_pool_tma.cuh)
 #endif
 #ifndef LTHC_BCAST_STAGES_16BIT
-#define LTHC_BCAST_STAGES_16BIT 6   // write family (this file)
+#define LTHC_BCAST_STAGES_16BIT 6   // write family (this file), L != 1
 #endif
+
 constexpr int kStripCells = LTHC_STRIP_CELLS;
 constexpr int kBoxCols = 4 * kStripCells;
-constexpr int kBcastConsumerWarps = 4;
-constexpr int kBcastThreads = 32 * (kBcastConsumerWarps + 1);
 
-template <typename T, int LMAX>
+// Consumer shape of the write-family kernel for a layer count and base.  Deep
+// stacks (L = 12) keep one warp per cell row holding the weights of all 4
+// columns in registers (each update pair loaded from shared memory feeds 4
+// FMAs), two CTAs per SM.  A single update with a base (write_add) has almost
+// no arithmetic and is bound by bytes in flight: one warp per cell (row,
+// column) and a single CTA per SM with a deep ring.  Without a base (write, the
+// read backward's grad_x) the loads are small and the output stores dominate:
+// several CTAs per SM, each with several tile stores in flight (kStoreLag).
+#ifndef LTHC_BCAST1_COLS
+#define LTHC_BCAST1_COLS 1
+#endif
+#ifndef LTHC_BCAST1_MIN_BLOCKS
+#define LTHC_BCAST1_MIN_BLOCKS 1
+#endif
+#ifndef LTHC_BCAST1_STAGES_16BIT
+#define LTHC_BCAST1_STAGES_16BIT 15
+#endif
+#ifndef LTHC_BCAST_COLS
+#define LTHC_BCAST_COLS 4
+#endif
+#ifndef LTHC_BCAST_MIN_BLOCKS
+#define LTHC_BCAST_MIN_BLOCKS 3
+#endif
+#ifndef LTHC_BCAST_NOBASE_STORE_LAG
+#define LTHC_BCAST_NOBASE_STORE_LAG 1
+#endif
+#ifndef LTHC_BCAST_BASE_STORE_LAG
+#define LTHC_BCAST_BASE_STORE_LAG 1
+#endif
+template <int LT, bool HAS_BASE>
+struct BcastShape {
+  static constexpr bool kSingle = LT == 1 && HAS_BASE;
+  static constexpr int kCols = kSingle ? LTHC_BCAST1_COLS : LTHC_BCAST_COLS;  // cell columns per consumer warp
+  static constexpr int kWarpsPerRow = 4 / kCols;
+  static_assert(kCols * kWarpsPerRow == 4, "columns per warp must divide 4");
+  static constexpr int kConsumerWarps = 4 * kWarpsPerRow;
+  static constexpr int kThreads = 32 * (kConsumerWarps + 1);
+  static constexpr int kMinBlocks = kSingle ? LTHC_BCAST1_MIN_BLOCKS : LTHC_BCAST_MIN_BLOCKS;
+  static constexpr int kStages16 = kSingle ? LTHC_BCAST1_STAGES_16BIT : LTHC_BCAST_STAGES_16BIT;
+  // Output tile stores a CTA keeps in flight before it recycles a stage.
+  static constexpr int kStoreLag = HAS_BASE ? LTHC_BCAST_BASE_STORE_LAG : LTHC_BCAST_NOBASE_STORE_LAG;
+};
+
+template <typename T, int LT, bool HAS_BASE>
 struct BcastLayout {
+  using Shape = BcastShape<LT, HAS_BASE>;
+  static constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
   static constexpr int kBaseBytes = 4 * kBoxCols * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kDzTileBytes = kStripCells * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kStageBytes = kBaseBytes + LMAX * kDzTileBytes;
-  static constexpr int kStages = sizeof(T) == 2 ? LTHC_BCAST_STAGES_16BIT : (LTHC_BCAST_STAGES_16BIT + 1) / 2;
+  static constexpr int kStages = sizeof(T) == 2 ? Shape::kStages16 : (Shape::kStages16 + 1) / 2;
+  static_assert(Shape::kStoreLag >= 1 && Shape::kStoreLag < kStages, "store lag must be below the stage count");
   static constexpr int kBarrierOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarrierOffset + 2 * kStages * 8 + 128;  // + alignment slack
+  static_assert(kSmemBytes <= 227 * 1024, "write-family stages exceed the shared memory of a CTA");
 };
 
 struct BcastTmaParams {
@@ -95,9 +142,11 @@ struct StripCursor {
 };
 
 template <typename T, int LT, bool HAS_BASE>
-__global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const __grid_constant__ BcastTmaParams p) {
+__global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape<LT, HAS_BASE>::kMinBlocks)
+    broadcast_tma_kernel(const __grid_constant__ BcastTmaParams p) {
   constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
-  using Lay = BcastLayout<T, LMAX>;
+  using Lay = BcastLayout<T, LT, HAS_BASE>;
+  using Shape = typename Lay::Shape;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarrierOffset);
@@ -120,7 +169,7 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
   }
   __syncthreads();
 
-  if (warp == kBcastConsumerWarps) {
+  if (warp == Shape::kConsumerWarps) {
     // ---------------- producer: one elected lane issues every TMA load ----------
     if (lane == 0) {
       if constexpr (HAS_BASE) prefetch_tmap(&p.tm_base);
@@ -156,23 +205,24 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
     }
     return;
   }
-
   // ---------------- consumers ---------------------------------------------------
   // Each lane computes its 4 columns x cells of the strip in place over the staged
   // base tile; then one elected thread writes the whole tile with a TMA store
   // (which clips columns past the residual edge and channels past C) and hands
   // the stage back to the producer once the store has read it.
-  const int row = warp;
+  constexpr int kCols = Shape::kCols;
+  const int row = warp / Shape::kWarpsPerRow;
+  const int col0 = (warp % Shape::kWarpsPerRow) * kCols;
   const int64_t c = c0 + 2 * lane;
   const bool cvalid = c < p.C;
-  float2 w[LMAX][4];
+  float2 w[LMAX][kCols];
 #pragma unroll
   for (int l = 0; l < LMAX; ++l) {
 #pragma unroll
-    for (int col = 0; col < 4; ++col) {
+    for (int col = 0; col < kCols; ++col) {
       if (cvalid && l < L) {
-        w[l][col].x = load_weight(p.w[l], p.w_dtype, c * kPos + row * 4 + col);
-        w[l][col].y = load_weight(p.w[l], p.w_dtype, (c + 1) * kPos + row * 4 + col);
+        w[l][col].x = load_weight(p.w[l], p.w_dtype, c * kPos + row * 4 + col0 + col);
+        w[l][col].y = load_weight(p.w[l], p.w_dtype, (c + 1) * kPos + row * 4 + col0 + col);
       } else {
         w[l][col] = make_float2(0.f, 0.f);
       }
@@ -189,10 +239,10 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
     const uint32_t sb = smem_base + s * Lay::kStageBytes;
 #pragma unroll
     for (int k = 0; k < kStripCells; ++k) {
-      float2 acc[4];
-      const uint32_t xa = sb + ((row * kBoxCols + 4 * k) * kSliceCh + 2 * lane) * kEs;
+      float2 acc[kCols];
+      const uint32_t xa = sb + ((row * kBoxCols + 4 * k + col0) * kSliceCh + 2 * lane) * kEs;
 #pragma unroll
-      for (int col = 0; col < 4; ++col) {
+      for (int col = 0; col < kCols; ++col) {
         if constexpr (HAS_BASE)
           acc[col] = lds_pair<T>(xa + col * kSliceCh * kEs);
         else
@@ -203,20 +253,21 @@ __global__ void __launch_bounds__(kBcastThreads, 3) broadcast_tma_kernel(const _
         if (l < L) {
           const float2 d = lds_pair<T>(sb + Lay::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-          for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
+          for (int col = 0; col < kCols; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
         }
       }
 #pragma unroll
-      for (int col = 0; col < 4; ++col) sts_pair<T>(xa + col * kSliceCh * kEs, acc[col]);
+      for (int col = 0; col < kCols; ++col) sts_pair<T>(xa + col * kSliceCh * kEs, acc[col]);
     }
     fence_proxy_async_smem();
-    named_barrier(1, 32 * kBcastConsumerWarps);
+    named_barrier(1, 32 * Shape::kConsumerWarps);
     if (storer) {
       tma_store_4d(&p.tm_out, smem + s * Lay::kStageBytes, static_cast<int32_t>(c0), 4 * cur.wx0(), 4 * cur.wy,
                    static_cast<int32_t>(cur.b));
       bulk_commit();
-      bulk_wait_read<1>();  // the previous stage's store has read its tile
-      if (it > 0) mbar_arrive(&empty[(it - 1) % Lay::kStages]);
+      // The store issued kStoreLag strips ago has read its tile: recycle that stage.
+      bulk_wait_read<Shape::kStoreLag>();
+      if (it >= Shape::kStoreLag) mbar_arrive(&empty[(it - Shape::kStoreLag) % Lay::kStages]);
     }
   }
   if (storer) bulk_wait_all();
