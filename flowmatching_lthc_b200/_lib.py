@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_int, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("liblthc_b200.so")
@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_lazy_update_fwd": (_I, [_P, _P, _P, _I, _P, _I, _P, _L, _L, _I, _P]),
     "lthc_lazy_update_bwd_workspace_bytes": (c_size_t, [_L, _L]),
     "lthc_lazy_update_bwd": (_I, [_P, _P, _P, _I, _P, _I, _P, _P, _P, _P, c_size_t, _L, _L, _I, _P]),
+    "lthc_final_norm_modulate_fwd": (_I, [_P, _P, _I, _P, _P, _L, _P, _L, _L, _L, c_float, _I, _P]),
+    "lthc_final_norm_modulate_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
+    "lthc_final_norm_modulate_bwd": (_I, [_P, _P, _I, _P, _L, _P, _P, _P, _P, _P, _P, c_size_t, _L, _L, _L,
+                                          c_float, _I, _P]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -7,6 +7,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include <cudaTypedefs.h>
@@ -17,6 +18,7 @@
 #include "lthc_tma.cuh"
 #include "lthc_broadcast_tma.cuh"
 #include "lthc_pool_tma.cuh"
+#include "lthc_final.cuh"
 
 namespace lthc {
 
@@ -231,20 +233,28 @@ int encode_workspace_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t 
   return LTHC_OK;
 }
 
-// Per-device, per-kernel one-time set-up: opt in to the dynamic shared memory the
-// kernel needs and record how many CTAs fit on one SM.
+// Per-device, per-kernel, per-launch-shape set-up (cached): opt in to the dynamic
+// shared memory the launch needs (the attribute only ever grows, so launches of
+// the same kernel with other shapes stay valid) and record how many CTAs of that
+// shape fit on one SM.
 template <typename Kernel>
 int resident_ctas(Kernel kern, int threads, int smem_bytes, int* out) {
   static std::mutex mu;
-  static std::map<std::pair<int, const void*>, int> cache;
+  static std::map<std::tuple<int, const void*, int, int>, int> cache;
+  static std::map<std::pair<int, const void*>, int> smem_set;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return launched("cudaGetDevice");
-  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
+  const void* fn = reinterpret_cast<const void*>(kern);
+  const auto key = std::make_tuple(dev, fn, threads, smem_bytes);
   std::lock_guard<std::mutex> lk(mu);
   auto it = cache.find(key);
   if (it == cache.end()) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
-      return launched("cudaFuncSetAttribute");
+    int& cur = smem_set[std::make_pair(dev, fn)];
+    if (smem_bytes > cur) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+        return launched("cudaFuncSetAttribute");
+      cur = smem_bytes;
+    }
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem_bytes) != cudaSuccess)
       return launched("cudaOccupancyMaxActiveBlocksPerMultiprocessor");
@@ -401,6 +411,116 @@ int read_family(const ReadJob& j, size_t ws_bytes, int act, cudaStream_t s) {
 int check_weight_dtype(int dt, const char* name) {
   if (!valid_act(dt)) return fail(LTHC_ERR_DTYPE, "unknown %s dtype code %d", name, dt);
   return LTHC_OK;
+}
+
+// ---- final-layer prologue (RMSNorm + modulate) --------------------------------
+
+// Launch shape: one thread per channel pair (at least 4 warps); tiles of two
+// tokens per warp (forward) or one (backward, two tensors per token), 3 tiles in
+// flight; the tile shrinks for wide rows so that a CTA's ring stays within
+// kFinalSmemBudget (two CTAs per SM).
+struct FinalShape {
+  int threads, tile, stages;
+  size_t smem;
+};
+constexpr size_t kFinalSmemBudget = 100 * 1024;
+
+FinalShape final_shape(int64_t C, int es, bool bwd) {
+  FinalShape f;
+  const int warps = static_cast<int>(std::min<int64_t>(kFinalMaxThreads / 32, std::max<int64_t>(4, ceil_div(C, 64))));
+  f.threads = 32 * warps;
+  f.stages = 3;
+  f.tile = bwd ? warps : 2 * warps;
+  while (f.tile > 1 && FinalSmem(C, es, f.tile, f.stages, bwd).total > kFinalSmemBudget) --f.tile;
+  f.smem = FinalSmem(C, es, f.tile, f.stages, bwd).total;
+  return f;
+}
+
+// CTAs per image: about two per SM over the whole batch, each with whole tiles.
+// The backward's workspace is sized with tile = 1 (an upper bound on the count).
+constexpr int kFinalCtasPerSm = 2;
+
+int64_t final_tokens_per_cta(int64_t B, int64_t T, int tile, int sms) {
+  const int64_t want = std::max<int64_t>(1, static_cast<int64_t>(sms) * kFinalCtasPerSm / std::max<int64_t>(B, 1));
+  const int64_t k = std::max<int64_t>(1, std::min<int64_t>(want, ceil_div(T, tile)));
+  return ceil_div(ceil_div(T, k), tile) * tile;
+}
+
+int64_t final_ctas_per_image(int64_t B, int64_t T, int tile, int sms) {
+  if (T <= 0) return 1;
+  return ceil_div(T, final_tokens_per_cta(B, T, tile, sms));
+}
+
+size_t final_ws_bytes(int64_t B, int64_t T, int64_t C, int sms) {
+  if (B <= 0 || T <= 0) return 0;
+  return static_cast<size_t>(B * final_ctas_per_image(B, T, 1, sms)) * 3 * C * sizeof(float);
+}
+
+int check_final(int64_t B, int64_t T, int64_t C, int64_t mod_stride, int act_dtype, int w_dtype, float eps) {
+  if (B < 0 || T < 0) return fail(LTHC_ERR_SHAPE, "batch and tokens must be >= 0, got %lld, %lld", (long long)B,
+                                  (long long)T);
+  if (B > 65535) return fail(LTHC_ERR_SHAPE, "batch must be <= 65535, got %lld", (long long)B);
+  if (C < 8 || C > kFinalChunk * kFinalMaxChunks || C % 8 != 0)
+    return fail(LTHC_ERR_SHAPE, "channels must be a multiple of 8 in [8, %d], got %lld", kFinalChunk * kFinalMaxChunks,
+                (long long)C);
+  if (mod_stride < C) return fail(LTHC_ERR_SHAPE, "shift/scale row stride %lld is below C = %lld",
+                                  (long long)mod_stride, (long long)C);
+  if (!valid_act(act_dtype)) return fail(LTHC_ERR_DTYPE, "unknown activation dtype code %d", act_dtype);
+  if (!valid_act(w_dtype)) return fail(LTHC_ERR_DTYPE, "unknown norm weight dtype code %d", w_dtype);
+  if (!(eps >= 0.f)) return fail(LTHC_ERR_SHAPE, "eps must be >= 0");
+  return LTHC_OK;
+}
+
+template <typename T, bool BWD>
+int final_launch(FinalParams& p, int64_t B, int sms, int64_t* ctas_per_image, cudaStream_t s) {
+  const FinalShape f = final_shape(p.C, sizeof(T), BWD);
+  p.tile = f.tile;
+  p.stages = f.stages;
+  auto go = [&](auto kern) -> int {
+    int per_sm = 0;
+    LTHC_TRY(resident_ctas(kern, f.threads, static_cast<int>(f.smem), &per_sm));
+    // forward: one wave of resident CTAs; backward: the workspace plan's count
+    const int ctas_per_sm = BWD ? kFinalCtasPerSm : per_sm;
+    p.tokens_per_cta = final_tokens_per_cta(B, p.T, f.tile, sms * ctas_per_sm / kFinalCtasPerSm);
+    const int64_t K = ceil_div(p.T, p.tokens_per_cta);
+    *ctas_per_image = K;
+    const dim3 grid(static_cast<unsigned>(K), static_cast<unsigned>(B));
+    kern<<<grid, f.threads, f.smem, s>>>(p);
+    return launched(BWD ? "final norm/modulate backward" : "final norm/modulate forward");
+  };
+  switch (ceil_div(p.C, kFinalChunk)) {
+    case 1: return go(final_norm_modulate_kernel<T, BWD, 1>);
+    case 2: return go(final_norm_modulate_kernel<T, BWD, 2>);
+    case 3: return go(final_norm_modulate_kernel<T, BWD, 3>);
+    default: return go(final_norm_modulate_kernel<T, BWD, 4>);
+  }
+}
+
+template <bool BWD>
+int final_dispatch(FinalParams& p, int64_t B, int sms, int64_t* K, int act, cudaStream_t s) {
+  switch (act) {
+    case LTHC_DTYPE_F32: return final_launch<float, BWD>(p, B, sms, K, s);
+    case LTHC_DTYPE_BF16: return final_launch<__nv_bfloat16, BWD>(p, B, sms, K, s);
+    default: return final_launch<__half, BWD>(p, B, sms, K, s);
+  }
+}
+
+FinalParams final_params(const void* x, const void* w, int w_dtype, const void* shift, const void* scale,
+                         int64_t mod_stride, int64_t T, int64_t C, float eps) {
+  FinalParams p;
+  memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.w = w;
+  p.w_dtype = w_dtype;
+  p.shift = shift;
+  p.scale = scale;
+  p.mod_stride = mod_stride;
+  p.T = T;
+  p.C = C;
+  p.eps = eps;
+  p.inv_c = 1.0f / static_cast<float>(C);
+  p.c_f = static_cast<float>(C);
+  return p;
 }
 
 }  // namespace
@@ -754,6 +874,73 @@ int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alp
     lazy_bwd_finalize_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(p, static_cast<int>(nblk),
                                                                                       grad_alpha, grad_beta);
     LTHC_TRY(launched("lazy update backward finalize"));
+  }
+  return LTHC_OK;
+}
+
+// ------------------------- final-layer prologue --------------------------------
+
+int lthc_final_norm_modulate_fwd(const void* x, const void* norm_weight, int w_dtype, const void* shift,
+                                 const void* scale, int64_t mod_stride, void* out, int64_t B, int64_t T, int64_t C,
+                                 float eps, int act_dtype, void* stream) {
+  LTHC_TRY(check_final(B, T, C, mod_stride, act_dtype, w_dtype, eps));
+  const bool nonempty = B > 0 && T > 0;
+  LTHC_TRY(check_act(x, "x", nonempty));
+  LTHC_TRY(check_act(out, "out", nonempty));
+  if (!norm_weight || !shift || !scale) return fail(LTHC_ERR_NULL_POINTER, "norm_weight, shift and scale must be set");
+  if (!nonempty) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  FinalParams p = final_params(x, norm_weight, w_dtype, shift, scale, mod_stride, T, C, eps);
+  p.out = out;
+  int64_t K = 0;
+  return final_dispatch<false>(p, B, sms, &K, act_dtype, static_cast<cudaStream_t>(stream));
+}
+
+size_t lthc_final_norm_modulate_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C) {
+  if (C <= 0) return 0;
+  return final_ws_bytes(B, T, C, sms_for_sizing());
+}
+
+int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight, int w_dtype, const void* scale,
+                                 int64_t mod_stride, const void* grad_out, void* grad_x, float* grad_weight,
+                                 float* grad_shift, float* grad_scale, void* workspace, size_t workspace_bytes,
+                                 int64_t B, int64_t T, int64_t C, float eps, int act_dtype, void* stream) {
+  LTHC_TRY(check_final(B, T, C, mod_stride, act_dtype, w_dtype, eps));
+  const bool nonempty = B > 0 && T > 0;
+  LTHC_TRY(check_act(x, "x", nonempty));
+  LTHC_TRY(check_act(grad_out, "grad_out", nonempty));
+  LTHC_TRY(check_act(grad_x, "grad_x", nonempty));
+  if (!norm_weight || !scale) return fail(LTHC_ERR_NULL_POINTER, "norm_weight and scale must be set");
+  if (!nonempty && !grad_weight && (B == 0 || (!grad_shift && !grad_scale))) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!nonempty) {
+    if (grad_weight && cudaMemsetAsync(grad_weight, 0, sizeof(float) * C, s) != cudaSuccess) return launched("memset");
+    if (B > 0 && grad_shift && cudaMemsetAsync(grad_shift, 0, sizeof(float) * B * C, s) != cudaSuccess)
+      return launched("memset");
+    if (B > 0 && grad_scale && cudaMemsetAsync(grad_scale, 0, sizeof(float) * B * C, s) != cudaSuccess)
+      return launched("memset");
+    return LTHC_OK;
+  }
+  const size_t need = final_ws_bytes(B, T, C, sms);
+  if (!workspace || workspace_bytes < need)
+    return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                need);
+  if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+  FinalParams p = final_params(x, norm_weight, w_dtype, nullptr, scale, mod_stride, T, C, eps);
+  p.grad_out = grad_out;
+  p.out = grad_x;
+  p.partial = static_cast<float*>(workspace);
+  int64_t K = 0;
+  LTHC_TRY(final_dispatch<true>(p, B, sms, &K, act_dtype, s));
+  if (grad_weight || grad_shift || grad_scale) {
+    const int64_t total = C + 2 * B * C;
+    const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(sms) * 8);
+    final_bwd_finalize_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p.partial, grad_weight, grad_shift,
+                                                                             grad_scale, B, K, C);
+    LTHC_TRY(launched("final norm/modulate backward finalize"));
   }
   return LTHC_OK;
 }

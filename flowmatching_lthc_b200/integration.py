@@ -15,6 +15,7 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   SharedReadLocalTHCSharedAdaLNJiT.final_accumulate_reference    :1368-1372 (pure-torch loop)
   SharedReadFusedFinalLocalTHCSharedAdaLNJiT.final_accumulate_reference   :1407-1410 (stacked op)
   SharedReadFusedFinal12LocalTHCSharedAdaLNJiT.final_accumulate_reference :1416-1420 (released op)
+  FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
 
 Shape checks and messages are the reference's own; the arithmetic runs in
 ``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
@@ -84,6 +85,18 @@ def _final12(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tenso
     return ops.materialise(x0, list(dz_list), betas)
 
 
+def _final_layer(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
+    shift, scale = t2.chunk(2, dim=1)
+    norm = self.norm_final
+    if x.dtype != shift.dtype or x.dim() != 3 or x.shape[-1] > ops.FINAL_MAX_CHANNELS:
+        # a dtype mix the fused kernel does not take: the reference's own expression
+        return self.linear(_ORIGINAL_MODULATE(norm(x), shift, scale))
+    return self.linear(ops.final_norm_modulate(x, norm.weight, shift, scale, norm.eps))
+
+
+_ORIGINAL_MODULATE = None
+
+
 PATCHES = (
     ("SharedLocalRead", "read", _read),
     ("LayerLocalWrite", "write", _write),
@@ -92,6 +105,7 @@ PATCHES = (
     ("SharedReadLocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final_loop),
     ("SharedReadFusedFinalLocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final_stacked),
     ("SharedReadFusedFinal12LocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final12),
+    ("FinalLayerSharedAdaLN", "forward", _final_layer),
 )
 
 
@@ -119,6 +133,8 @@ def install(local_thc: ModuleType | None = None) -> Installation:
     """Route the reference model's LTHC methods through the B200 kernels."""
     if local_thc is None:
         local_thc = importlib.import_module("flowmatching_lthc.models.local_thc")
+    global _ORIGINAL_MODULATE
+    _ORIGINAL_MODULATE = local_thc.modulate
     inst = Installation(local_thc)
     for cls_name, meth, fn in PATCHES:
         cls = getattr(local_thc, cls_name, None)

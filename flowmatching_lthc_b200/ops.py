@@ -475,6 +475,106 @@ def _(high, low):
 
 
 # ---------------------------------------------------------------------------
+# final-layer prologue  m = modulate(RMSNorm(x), shift, scale)
+# (FinalLayerSharedAdaLN.forward, local_thc.py:865-873; RMSNorm,
+# jit_shared_adaln.py:20-30; modulate, local_thc.py:37-38)
+# ---------------------------------------------------------------------------
+FINAL_MAX_CHANNELS = 1024
+
+
+def _final_geom(x: Tensor, weight: Tensor, shift: Tensor, scale: Tensor, what: str) -> tuple[int, int, int]:
+    if x.dim() != 3:
+        raise ValueError(f"{what}: expected tokens [B,T,C], got {tuple(x.shape)}")
+    b, t, c = x.shape
+    if c % 8 != 0 or c < 8 or c > FINAL_MAX_CHANNELS:
+        raise ValueError(f"{what}: channel count {c} must be a multiple of 8 in [8, {FINAL_MAX_CHANNELS}]")
+    if tuple(weight.shape) != (c,):
+        raise ValueError(f"{what}: expected norm weight [{c}], got {tuple(weight.shape)}")
+    for name, m in (("shift", shift), ("scale", scale)):
+        if tuple(m.shape) != (b, c):
+            raise ValueError(f"{what}: expected {name} [{b},{c}], got {tuple(m.shape)}")
+        if m.dtype != x.dtype:
+            raise ValueError(f"{what}: {name} dtype {m.dtype} differs from the activation dtype {x.dtype}")
+    return b, t, c
+
+
+def _mod_rows(shift: Tensor, scale: Tensor) -> tuple[Tensor, Tensor, int]:
+    """shift / scale and their common row stride; the two halves of
+    ``t2.chunk(2, dim=1)`` pass through without a copy."""
+    c = shift.shape[1]
+    if (shift.stride(1) == 1 and scale.stride(1) == 1 and shift.stride(0) == scale.stride(0)
+            and shift.stride(0) >= c):
+        return shift, scale, shift.stride(0)
+    return shift.contiguous(), scale.contiguous(), c
+
+
+@torch.library.custom_op("lthc_b200::final_norm_modulate", mutates_args=(), device_types="cuda")
+def final_norm_modulate(x: Tensor, weight: Tensor, shift: Tensor, scale: Tensor, eps: float) -> Tensor:
+    """modulate(RMSNorm(x) with weight and eps, shift, scale) over tokens [B,T,C]."""
+    _require_cuda(x, weight, shift, scale)
+    b, t, c = _final_geom(x, weight, shift, scale, "final_norm_modulate")
+    x, weight = x.contiguous(), weight.contiguous()
+    sh, sc, stride = _mod_rows(shift, scale)
+    out = torch.empty_like(x)
+    with _guard(x):
+        _lib.call("lthc_final_norm_modulate_fwd", x.data_ptr(), weight.data_ptr(), _code(weight, "norm weight"),
+                  sh.data_ptr(), sc.data_ptr(), stride, out.data_ptr(), b, t, c, float(eps),
+                  _code(x, "final_norm_modulate"), _stream(x))
+    return out
+
+
+@final_norm_modulate.register_fake
+def _(x, weight, shift, scale, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("lthc_b200::final_norm_modulate_bwd", mutates_args=(), device_types="cuda")
+def final_norm_modulate_bwd(grad_out: Tensor, x: Tensor, weight: Tensor, scale: Tensor,
+                            eps: float) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """(grad_x, grad_weight fp32 [C], grad_shift fp32 [B,C], grad_scale fp32 [B,C])."""
+    _require_cuda(grad_out, x, weight, scale)
+    b, t, c = _final_geom(x, weight, scale, scale, "final_norm_modulate_bwd")
+    x, weight, g = x.contiguous(), weight.contiguous(), grad_out.to(x.dtype).contiguous()
+    _, sc, stride = _mod_rows(scale, scale)
+    gx = torch.empty_like(x)
+    gw = torch.empty((c,), device=x.device, dtype=torch.float32)
+    gsh = torch.empty((b, c), device=x.device, dtype=torch.float32)
+    gsc = torch.empty((b, c), device=x.device, dtype=torch.float32)
+    with _guard(x):
+        ws_bytes = _lib.load().lthc_final_norm_modulate_bwd_workspace_bytes(b, t, c)
+        ws = _workspace(ws_bytes, x.device)
+        _lib.call("lthc_final_norm_modulate_bwd", x.data_ptr(), weight.data_ptr(), _code(weight, "norm weight"),
+                  sc.data_ptr(), stride, g.data_ptr(), gx.data_ptr(), gw.data_ptr(), gsh.data_ptr(), gsc.data_ptr(),
+                  ws.data_ptr(), ws_bytes, b, t, c, float(eps), _code(x, "final_norm_modulate_bwd"), _stream(x))
+    return gx, gw, gsh, gsc
+
+
+@final_norm_modulate_bwd.register_fake
+def _(grad_out, x, weight, scale, eps):
+    b, _, c = x.shape
+    f32 = dict(dtype=torch.float32)
+    return torch.empty_like(x), x.new_empty((c,), **f32), x.new_empty((b, c), **f32), x.new_empty((b, c), **f32)
+
+
+def _final_setup(ctx, inputs, output):
+    x, weight, shift, scale, eps = inputs
+    ctx.eps = eps
+    ctx.shift_dtype = shift.dtype
+    ctx.save_for_backward(x, weight, scale)
+
+
+def _final_backward(ctx, grad_out):
+    x, weight, scale = ctx.saved_tensors
+    need_x, need_w, need_sh, need_sc, _ = ctx.needs_input_grad
+    gx, gw, gsh, gsc = final_norm_modulate_bwd(grad_out, x, weight, scale, ctx.eps)
+    return ((gx if need_x else None), (gw.to(weight.dtype) if need_w else None),
+            (gsh.to(ctx.shift_dtype) if need_sh else None), (gsc.to(scale.dtype) if need_sc else None), None)
+
+
+final_norm_modulate.register_autograd(_final_backward, setup_context=_final_setup)
+
+
+# ---------------------------------------------------------------------------
 # Mirrors of the reference jit_thc:: Triton op surface (same names and argument
 # order; "local_write" = read and "local_read" = write are that file's legacy
 # names, local_thc_triton_kernels.py:2673-2723).

@@ -216,6 +216,34 @@ LTHC_API int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const 
                          size_t workspace_bytes, int64_t N, int64_t C, int act_dtype,
                          void* stream);
 
+/* ======================= final-layer prologue on the residual =============== */
+
+/* m[b,t,:] = modulate(RMSNorm(x[b,t,:]), shift[b,:], scale[b,:]) over the
+ * materialised residual x [B, T, C] (T = tokens per image), i.e.
+ *   n = (x * rsqrt(mean_c(x^2) + eps) * norm_weight)   in fp32, rounded to the activation dtype
+ *   m = n * (1 + scale[b]) + shift[b]                   each op rounded to the activation dtype
+ * shift / scale are rows of row stride mod_stride (elements) in the activation
+ * dtype (the two halves of t2 = shared_final_modulation(c)); norm_weight is [C]
+ * of w_dtype.  C is a multiple of 8, at most 1024.  Replaces the eager
+ * norm_final + modulate of FinalLayerSharedAdaLN.forward (local_thc.py:865-873;
+ * RMSNorm jit_shared_adaln.py:20-30; modulate local_thc.py:37-38); the final
+ * Linear stays a library GEMM. */
+LTHC_API int lthc_final_norm_modulate_fwd(const void* x, const void* norm_weight, int w_dtype,
+                         const void* shift, const void* scale, int64_t mod_stride, void* out,
+                         int64_t B, int64_t T, int64_t C, float eps, int act_dtype, void* stream);
+
+/* Backward of lthc_final_norm_modulate_fwd given grad_out = dL/dm:
+ *   grad_x [B,T,C] (activation dtype), and, each optional (NULL: not computed),
+ *   grad_weight [C], grad_shift [B,C], grad_scale [B,C] as fp32 sums over tokens
+ *   (fixed order, run-to-run reproducible).
+ * Follows the reference autograd of the same expression op by op. */
+LTHC_API size_t lthc_final_norm_modulate_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C);
+LTHC_API int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight, int w_dtype,
+                         const void* scale, int64_t mod_stride, const void* grad_out, void* grad_x,
+                         float* grad_weight, float* grad_shift, float* grad_scale, void* workspace,
+                         size_t workspace_bytes, int64_t B, int64_t T, int64_t C, float eps,
+                         int act_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

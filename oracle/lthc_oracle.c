@@ -17,6 +17,9 @@
  *   oracle_weight_grad     _cell_weight_grad_kernel          local_thc_triton_kernels.py:167-199
  *   oracle_lazy_fwd        lazy_workspace_update + gamma     local_thc.py:1278-1283, 1325-1328
  *   oracle_lazy_bwd        autograd of the two lines above
+ *   oracle_final_fwd       FinalLayerSharedAdaLN.forward     local_thc.py:865-873 (RMSNorm
+ *                          jit_shared_adaln.py:20-30, modulate local_thc.py:37-38), without its Linear
+ *   oracle_final_bwd       autograd of the line above
  *
  * Arithmetic: inputs are widened to fp32 exactly; per-element sums over the 16
  * cell positions or the L layers accumulate in fp32 with fused multiply-add in
@@ -29,6 +32,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -266,4 +270,103 @@ void oracle_lazy_bwd(const void* gzo, const void* dz, const void* a, int adt, co
       if (gb) gb[c * 16 + r] = s * ld(a, adt, c * 16 + r);
     }
   }
+}
+
+/* ---- final-layer prologue ---------------------------------------------------
+ * FinalLayerSharedAdaLN.forward (local_thc.py:865-873) without its Linear:
+ *   RMSNorm (jit_shared_adaln.py:20-30): xf = x.float();
+ *     r = rsqrt(mean(xf^2) + eps); n = (xf * r * w).to(dtype)
+ *   modulate (local_thc.py:37-38): m = n * (1 + scale[b]) + shift[b], each op
+ *     rounded to the activation dtype (torch's 16-bit elementwise rule).
+ * The mean of squares is summed in fp64 and rounded once; rsqrt is evaluated in
+ * fp64 and rounded.  x/out: [B, T, C]; w: [C] (wdt); shift/scale: rows of
+ * stride ms (elements) in the activation dtype. */
+static inline float rnd(float v, int dt) {
+  if (dt == DT_BF16) return bf16_to_f32(f32_to_bf16(v));
+  if (dt == DT_F16) return f16_to_f32(f32_to_f16(v));
+  return v;
+}
+
+static inline float token_rstd(const void* x, int dt, int64_t row, int64_t C, float eps) {
+  double ss = 0.0;
+  for (int64_t c = 0; c < C; ++c) {
+    float v = ld(x, dt, row + c);
+    ss += (double)(v * v);
+  }
+  float ms = (float)ss * (1.0f / (float)C);
+  return (float)(1.0 / sqrt((double)(ms + eps)));
+}
+
+void oracle_final_fwd(const void* x, const void* w, int wdt, const void* shift, const void* scale, int64_t ms,
+                      void* out, int64_t B, int64_t T, int64_t C, float eps, int dt) {
+#pragma omp parallel for schedule(static)
+  for (int64_t bt = 0; bt < B * T; ++bt) {
+    int64_t b = bt / T, row = bt * C;
+    float r = token_rstd(x, dt, row, C, eps);
+    for (int64_t c = 0; c < C; ++c) {
+      float n = rnd((ld(x, dt, row + c) * r) * ld(w, wdt, c), dt);
+      float s1 = rnd(1.0f + ld(scale, dt, b * ms + c), dt);
+      float p = rnd(n * s1, dt);
+      st(out, dt, row + c, p + ld(shift, dt, b * ms + c));
+    }
+  }
+}
+
+/* Autograd of the expression above, op by op (torch derivative formulas):
+ *   g_n = (g_m * s1) rounded;  g_scale[b] = sum_t (g_m * n) rounded;  g_shift[b] = sum_t g_m
+ *   g_t = g_n * w;  g_w = sum_{b,t} g_n * t   (t = x * r)
+ *   g_r = sum_c g_t * x;  g_v = -0.5 * g_r * r^3;  g_sq = g_v / C
+ *   g_x = (g_t * r + g_sq * (2 x)) rounded to the activation dtype
+ * Sums over tokens and channels accumulate in fp64. */
+void oracle_final_bwd(const void* x, const void* w, int wdt, const void* scale, int64_t ms, const void* gm,
+                      void* gx, float* gw, float* gsh, float* gsc, int64_t B, int64_t T, int64_t C, float eps,
+                      int dt) {
+  float* rs = (float*)malloc(sizeof(float) * (size_t)(B * T > 0 ? B * T : 1));
+  if (!rs) return;
+#pragma omp parallel for schedule(static)
+  for (int64_t bt = 0; bt < B * T; ++bt) rs[bt] = token_rstd(x, dt, bt * C, C, eps);
+#pragma omp parallel for schedule(static)
+  for (int64_t bt = 0; bt < B * T; ++bt) {
+    int64_t b = bt / T, row = bt * C;
+    float r = rs[bt];
+    double dot = 0.0;
+    for (int64_t c = 0; c < C; ++c) {
+      float xv = ld(x, dt, row + c);
+      float s1 = rnd(1.0f + ld(scale, dt, b * ms + c), dt);
+      float gn = rnd(ld(gm, dt, row + c) * s1, dt);
+      dot += (double)((gn * ld(w, wdt, c)) * xv);
+    }
+    float gv = (-0.5f * (float)dot) * ((r * r) * r);
+    float gsq = gv / (float)C;
+    for (int64_t c = 0; c < C; ++c) {
+      float xv = ld(x, dt, row + c);
+      float s1 = rnd(1.0f + ld(scale, dt, b * ms + c), dt);
+      float gn = rnd(ld(gm, dt, row + c) * s1, dt);
+      float gt = gn * ld(w, wdt, c);
+      st(gx, dt, row + c, gt * r + gsq * (2.0f * xv));
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t c = 0; c < C; ++c) {
+    double aw = 0.0;
+    float wc = ld(w, wdt, c);
+    for (int64_t b = 0; b < B; ++b) {
+      double ash = 0.0, asc = 0.0;
+      float s1 = rnd(1.0f + ld(scale, dt, b * ms + c), dt);
+      for (int64_t t = 0; t < T; ++t) {
+        int64_t row = (b * T + t) * C;
+        float tt = ld(x, dt, row + c) * rs[b * T + t];
+        float n = rnd(tt * wc, dt);
+        float g = ld(gm, dt, row + c);
+        float gn = rnd(g * s1, dt);
+        ash += (double)g;
+        asc += (double)rnd(g * n, dt);
+        aw += (double)(gn * tt);
+      }
+      if (gsh) gsh[b * C + c] = (float)ash;
+      if (gsc) gsc[b * C + c] = (float)asc;
+    }
+    if (gw) gw[c] = (float)aw;
+  }
+  free(rs);
 }

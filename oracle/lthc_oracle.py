@@ -9,7 +9,7 @@ float16 (torch is used here only as a container; all arithmetic is in
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_int, c_int64, c_void_p
+from ctypes import c_float, c_int, c_int64, c_void_p
 from typing import Sequence
 
 import torch
@@ -36,6 +36,8 @@ def lib() -> ctypes.CDLL:
             "oracle_weight_grad": [p, ctypes.POINTER(p), i, p, i64, i64, i64, i],
             "oracle_lazy_fwd": [p, p, p, i, p, i, p, i64, i64, i],
             "oracle_lazy_bwd": [p, p, p, i, p, i, p, p, p, i64, i64, i],
+            "oracle_final_fwd": [p, p, i, p, p, i64, p, i64, i64, i64, c_float, i],
+            "oracle_final_bwd": [p, p, i, p, i64, p, p, p, p, p, i64, i64, i64, c_float, i],
             "oracle_num_threads": [],
             "oracle_set_num_threads": [i],
         }
@@ -176,5 +178,36 @@ def lazy_bwd(gzo: torch.Tensor, dz: torch.Tensor, alpha: torch.Tensor, beta: tor
     return gdz, ga, gb
 
 
+def _mod(shift: torch.Tensor, scale: torch.Tensor):
+    shift, scale = _c(shift), _c(scale)
+    return shift, scale, shift.shape[1]
+
+
+def final_fwd(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+              eps: float) -> torch.Tensor:
+    """FinalLayerSharedAdaLN.forward without its Linear (local_thc.py:865-873): modulate(RMSNorm(x))."""
+    x, weight = _c(x), _c(weight)
+    shift, scale, ms = _mod(shift, scale)
+    b, t, c = x.shape
+    out = torch.empty_like(x)
+    lib().oracle_final_fwd(_p(x), _p(weight), _DT[weight.dtype], _p(shift), _p(scale), ms, _p(out), b, t, c,
+                           float(eps), _DT[x.dtype])
+    return out
+
+
+def final_bwd(grad_out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor, eps: float):
+    """Autograd of final_fwd: (grad_x, grad_weight fp32 [C], grad_shift fp32 [B,C], grad_scale fp32 [B,C])."""
+    x, weight, gm = _c(x), _c(weight), _c(grad_out.to(x.dtype))
+    scale = _c(scale)
+    b, t, c = x.shape
+    gx = torch.empty_like(x)
+    gw = torch.empty(c, dtype=torch.float32)
+    gsh = torch.empty(b, c, dtype=torch.float32)
+    gsc = torch.empty(b, c, dtype=torch.float32)
+    lib().oracle_final_bwd(_p(x), _p(weight), _DT[weight.dtype], _p(scale), c, _p(gm), _p(gx), _p(gw), _p(gsh),
+                           _p(gsc), b, t, c, float(eps), _DT[x.dtype])
+    return gx, gw, gsh, gsc
+
+
 __all__ = ["lib", "num_threads", "set_num_threads", "read", "write", "write_add", "materialise", "materialise_bwd",
-           "weight_grad", "lazy_fwd", "lazy_bwd", "OUT"]
+           "weight_grad", "lazy_fwd", "lazy_bwd", "final_fwd", "final_bwd", "OUT"]

@@ -3,7 +3,7 @@ reference's own eager PyTorch code (tongtongliang/flowmatching_lthc) on CPU.
 
 Run from the repository root with the reference importable, e.g.
 
-    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py
+    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py [all|lthc|final]
 
 The reference is only needed to (re)generate the fixtures; the committed ``*.pt``
 files are what the tests read.  Every tensor is produced by the reference
@@ -14,6 +14,9 @@ functions named below (paths inside the reference repository):
   LayerLocalWrite.gamma_from_alpha       flowmatching_lthc/models/local_thc.py:1278-1283
   Block.lazy_workspace_update            flowmatching_lthc/models/local_thc.py:1325-1328
   Model.final_accumulate_reference       flowmatching_lthc/models/local_thc.py:1368-1372
+  FinalLayerSharedAdaLN (norm_final = RMSNorm, modulate, linear)
+                                         flowmatching_lthc/models/local_thc.py:37-38, 865-873
+                                         flowmatching_lthc/models/jit_shared_adaln.py:20-30
 
 Gradients come from torch.autograd through the same eager code.  Inputs follow
 the distributions of the benchmark configurations (X ~ N(0,1), read weights
@@ -108,6 +111,43 @@ def make_case(name: str, *, B: int, G: int, C: int, dtype: torch.dtype, depth: i
     return out
 
 
+def make_final_case(name: str, *, B: int, T: int, C: int, dtype: torch.dtype, seed: int) -> dict:
+    """FinalLayerSharedAdaLN's RMSNorm + modulate (and, in fp32, its whole forward
+    including the Linear) with autograd through the same eager code."""
+    gen = torch.Generator().manual_seed(seed)
+
+    def randn(*shape, mean=0.0, std=1.0):
+        return torch.randn(*shape, generator=gen) * std + mean
+
+    layer = L.FinalLayerSharedAdaLN(C, 4, 3)
+    with torch.no_grad():
+        layer.norm_final.weight.copy_(randn(C, mean=1.0, std=0.1))
+        layer.linear.weight.copy_(randn(48, C, std=0.02))
+        layer.linear.bias.copy_(randn(48, std=0.02))
+    x = randn(B, T, C).to(dtype)
+    t2 = randn(B, 2 * C, std=0.5).to(dtype)
+    g_m = randn(B, T, C).to(dtype)
+    out: dict = {"meta": {"name": name, "B": B, "T": T, "C": C, "dtype": str(dtype), "seed": seed,
+                          "eps": layer.norm_final.eps},
+                 "x": x, "t2": t2, "norm_weight": layer.norm_final.weight.detach().clone(), "g_m": g_m,
+                 "linear_weight": layer.linear.weight.detach().clone(), "linear_bias": layer.linear.bias.detach().clone()}
+    xr = x.clone().requires_grad_(True)
+    t2r = t2.clone().requires_grad_(True)
+    shift, scale = t2r.chunk(2, dim=1)
+    m = L.modulate(layer.norm_final(xr), shift, scale)
+    gx, gw, gt2 = torch.autograd.grad(m, (xr, layer.norm_final.weight, t2r), g_m)
+    out.update(m=m.detach(), gx=gx, g_norm_weight=gw, g_shift=gt2[:, :C].contiguous(), g_scale=gt2[:, C:].contiguous())
+    if dtype == torch.float32:
+        out["layer_out"] = layer(x, t2).detach()
+    return out
+
+
+FINAL_CASES = [
+    ("final_t64_c768_bf16", dict(B=2, T=64, C=768, dtype=torch.bfloat16, seed=10)),
+    ("final_t16_c40_f32", dict(B=3, T=16, C=40, dtype=torch.float32, seed=11)),
+    ("final_t8_c1024_bf16", dict(B=1, T=8, C=1024, dtype=torch.bfloat16, seed=12)),
+]
+
 CASES = [
     ("g4_c40_f32", dict(B=2, G=4, C=40, dtype=torch.float32, depth=12, seed=0)),
     ("g4_c40_bf16", dict(B=2, G=4, C=40, dtype=torch.bfloat16, depth=12, seed=1)),
@@ -116,13 +156,18 @@ CASES = [
 ]
 
 
-def main() -> None:
-    for name, kw in CASES:
-        case = make_case(name, **kw)
+def main(which: str = "all") -> None:
+    jobs = []
+    if which in ("all", "lthc"):
+        jobs += [(name, make_case, kw) for name, kw in CASES]
+    if which in ("all", "final"):
+        jobs += [(name, make_final_case, kw) for name, kw in FINAL_CASES]
+    for name, fn, kw in jobs:
+        case = fn(name, **kw)
         path = HERE / f"{name}.pt"
         torch.save(case, path)
         print(f"wrote {path} ({path.stat().st_size} bytes)")
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1] if len(sys.argv) > 1 else "all")

@@ -50,6 +50,13 @@ P = 256  # a 16-byte aligned non-null address that is never dereferenced
     (lambda L: L.lthc_materialise_fwd(P, None, None, 0, 12, P, 1, 16, 768, 1, None), 1),
     (lambda L: L.lthc_lazy_update_fwd(P, P, P, 0, P, 0, P, 4, 12, 1, None), 2),
     (lambda L: L.lthc_weight_grad(P, _lib.ptr_array([P]), 0, P, P, 1 << 20, 1, 16, 768, 1, None), 2),
+    (lambda L: L.lthc_final_norm_modulate_fwd(P, P, 0, P, P, 1536, P, 2, 4096, 1032, 1e-6, 1, None), 2),
+    (lambda L: L.lthc_final_norm_modulate_fwd(P, P, 0, P, P, 512, P, 2, 4096, 768, 1e-6, 1, None), 2),
+    (lambda L: L.lthc_final_norm_modulate_fwd(P, P, 7, P, P, 1536, P, 2, 4096, 768, 1e-6, 1, None), 3),
+    (lambda L: L.lthc_final_norm_modulate_fwd(P + 8, P, 0, P, P, 1536, P, 2, 4096, 768, 1e-6, 1, None), 4),
+    (lambda L: L.lthc_final_norm_modulate_fwd(P, None, 0, P, P, 1536, P, 2, 4096, 768, 1e-6, 1, None), 1),
+    (lambda L: L.lthc_final_norm_modulate_bwd(P, P, 0, P, 1536, P, None, None, None, None, P, 1 << 30, 2, 4096, 768,
+                                              1e-6, 1, None), 1),
 ])
 def test_validation_errors(call, status):
     lib = _lib.load()
@@ -64,6 +71,9 @@ def test_empty_batch_is_a_successful_no_op():
     assert lib.lthc_materialise12_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, P, 0, 16, 768, 1,
                                       None) == 0
     assert lib.lthc_lazy_update_fwd(P, P, P, 0, P, 0, P, 0, 768, 1, None) == 0
+    assert lib.lthc_final_norm_modulate_fwd(P, P, 0, P, P, 1536, P, 0, 4096, 768, 1e-6, 1, None) == 0
+    assert lib.lthc_final_norm_modulate_bwd(P, P, 0, P, 1536, P, P, None, None, None, None, 0, 0, 4096, 768, 1e-6, 1,
+                                            None) == 0
 
 
 def test_workspace_queries():
@@ -75,6 +85,9 @@ def test_workspace_queries():
     assert lib.lthc_weight_grad_workspace_bytes(64, 16, 768, 12) == n12
     assert lib.lthc_read_bwd_workspace_bytes(64, 16, 768) == n1
     assert lib.lthc_lazy_update_bwd_workspace_bytes(64 * 256, 768) % (768 * 4) == 0
+    assert lib.lthc_final_norm_modulate_bwd_workspace_bytes(0, 4096, 768) == 0
+    nf = lib.lthc_final_norm_modulate_bwd_workspace_bytes(64, 4096, 768)
+    assert nf > 0 and nf % (64 * 3 * 768 * 4) == 0
 
 
 def test_call_helper_raises_with_message():

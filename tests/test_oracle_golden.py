@@ -143,3 +143,47 @@ def test_output_rounding_matches_torch_casts():
         out = O.write(dz, beta)
         ref = cell_major_to_nhwc(dz.float()[:, :, None, :] * beta.t()[None, None]).to(dt)
         assert torch.equal(out.float(), ref.float())
+
+
+# ---- final-layer prologue (FinalLayerSharedAdaLN: RMSNorm + modulate) ----------
+FINAL_CASES = ["final_t64_c768_bf16", "final_t16_c40_f32", "final_t8_c1024_bf16"]
+
+
+def exact_fraction(a: torch.Tensor, b: torch.Tensor) -> float:
+    return (a == b).float().mean().item()
+
+
+@pytest.fixture(scope="module", params=FINAL_CASES)
+def final_case(request):
+    return torch.load(GOLDEN / f"{request.param}.pt")
+
+
+def test_final_norm_modulate_forward(final_case):
+    """Op-by-op rounding as the reference: the outputs agree exactly except where
+    the mean of squares, summed in another order, moves an element across a
+    rounding boundary of the activation dtype (16-bit); fp32 within 1e-5."""
+    c = final_case
+    C = c["meta"]["C"]
+    shift, scale = c["t2"][:, :C], c["t2"][:, C:]
+    m = O.final_fwd(c["x"], c["norm_weight"], shift, scale, c["meta"]["eps"])
+    assert m.dtype == c["m"].dtype
+    if m.dtype != torch.float32:  # fp32 has no output rounding to absorb the reduction order
+        assert exact_fraction(m, c["m"]) > 0.999
+    assert rel_err(m, c["m"]) < TOL[c["x"].dtype]
+    if "layer_out" in c:  # fp32: the full layer = Linear(m)
+        out = torch.nn.functional.linear(m, c["linear_weight"], c["linear_bias"])
+        assert rel_err(out, c["layer_out"]) < 1e-5
+
+
+def test_final_norm_modulate_backward(final_case):
+    c = final_case
+    C = c["meta"]["C"]
+    dt = c["x"].dtype
+    gx, gw, gsh, gsc = O.final_bwd(c["g_m"], c["x"], c["norm_weight"], c["t2"][:, C:], c["meta"]["eps"])
+    if dt != torch.float32:
+        assert exact_fraction(gx, c["gx"]) > 0.99
+    assert rel_err(gx, c["gx"]) < TOL[dt]
+    assert rel_err(gw, c["g_norm_weight"]) < 1e-5
+    # shift / scale gradients are sums over tokens, rounded once to the parameter dtype
+    assert rel_err(gsh.to(dt), c["g_shift"]) < TOL[dt]
+    assert rel_err(gsc.to(dt), c["g_scale"]) < TOL[dt]
