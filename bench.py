@@ -202,10 +202,22 @@ def op_step(op: str, cfg: dict):
         "lazy_bwd": (lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 2,
                      "lazy_bwd_kernel<bf16> + lazy_bwd_finalize_kernel"),
     }
+    if op in ("final_fwd", "final_bwd"):
+        # final-layer prologue on the materialised residual [B, 4096, 768] (FinalLayerSharedAdaLN)
+        T = 16 * G * G
+        xt, gm = x0.reshape(B, T, C), g.reshape(B, T, C)
+        nw = torch.ones(C, device=x0.device) + 0.1 * torch.randn(C, device=x0.device)
+        t2 = (0.5 * torch.randn(B, 2 * C, device=x0.device)).to(torch.bfloat16)
+        sh, sc = t2.chunk(2, dim=1)
+        table["final_fwd"] = (lambda: ops.final_norm_modulate(xt, nw, sh, sc, 1e-6), W.final_fwd_bytes(B, T, C, 2), 1,
+                              "final_norm_modulate_kernel<bf16, fwd>")
+        table["final_bwd"] = (lambda: ops.final_norm_modulate_bwd(gm, xt, nw, sc, 1e-6), W.final_bwd_bytes(B, T, C, 2),
+                              2, "final_norm_modulate_kernel<bf16, bwd> + final_bwd_finalize_kernel")
     return table[op]
 
 
-OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd")
+OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
+       "final_fwd", "final_bwd")
 MODEL_OPS = ("model_fwd", "train_step", "sample")
 # Largest batch per model call for which the reference Triton materialisation's
 # 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
@@ -384,6 +396,8 @@ WORKLOADS = {
     "write_add_fwd": "write_add X + P(dZ), config 2 shapes",
     "lazy_fwd": "lazy update Z + Gamma*dZ, config 2 shapes",
     "lazy_bwd": "lazy update bwd, config 2 shapes",
+    "final_fwd": "final-layer RMSNorm + AdaLN modulate on X_L [B, 4096, 768], config 2 shapes",
+    "final_bwd": "final-layer RMSNorm + modulate bwd (grad X_L, grad norm weight / shift / scale), config 2 shapes",
 }
 
 

@@ -416,21 +416,35 @@ int check_weight_dtype(int dt, const char* name) {
 // ---- final-layer prologue (RMSNorm + modulate) --------------------------------
 
 // Launch shape: one thread per channel pair (at least 4 warps); tiles of two
-// tokens per warp (forward) or one (backward, two tensors per token), 3 tiles in
-// flight; the tile shrinks for wide rows so that a CTA's ring stays within
-// kFinalSmemBudget (two CTAs per SM).
+// tokens per warp (forward) or one (backward, two tensors per token), 3 stages;
+// the tile shrinks for wide rows so that a CTA's ring stays within
+// kFinalSmemBudget (two CTAs per SM).  Measured on B200 at B = 64, T = 4096,
+// C = 768 bf16: 3 stages beat 4 or 6 (bigger tiles amortise the per-tile
+// barrier), and a 72 KB budget (3 CTAs per SM, smaller tiles) is slower.
 struct FinalShape {
   int threads, tile, stages;
   size_t smem;
 };
-constexpr size_t kFinalSmemBudget = 100 * 1024;
+#ifndef LTHC_FINAL_SMEM_BUDGET_KB
+#define LTHC_FINAL_SMEM_BUDGET_KB 110
+#endif
+#ifndef LTHC_FINAL_FWD_TOKENS_PER_WARP
+#define LTHC_FINAL_FWD_TOKENS_PER_WARP 2
+#endif
+#ifndef LTHC_FINAL_FWD_STAGES
+#define LTHC_FINAL_FWD_STAGES 3
+#endif
+#ifndef LTHC_FINAL_BWD_STAGES
+#define LTHC_FINAL_BWD_STAGES 3
+#endif
+constexpr size_t kFinalSmemBudget = LTHC_FINAL_SMEM_BUDGET_KB * 1024;
 
 FinalShape final_shape(int64_t C, int es, bool bwd) {
   FinalShape f;
   const int warps = static_cast<int>(std::min<int64_t>(kFinalMaxThreads / 32, std::max<int64_t>(4, ceil_div(C, 64))));
   f.threads = 32 * warps;
-  f.stages = 3;
-  f.tile = bwd ? warps : 2 * warps;
+  f.stages = bwd ? LTHC_FINAL_BWD_STAGES : LTHC_FINAL_FWD_STAGES;
+  f.tile = bwd ? warps : LTHC_FINAL_FWD_TOKENS_PER_WARP * warps;
   while (f.tile > 1 && FinalSmem(C, es, f.tile, f.stages, bwd).total > kFinalSmemBudget) --f.tile;
   f.smem = FinalSmem(C, es, f.tile, f.stages, bwd).total;
   return f;

@@ -23,11 +23,11 @@
 //   phase 1  one warp per token: the token's sums over channels (mean of
 //            squares -> r; backward: the dot product of grad t and x), lane l
 //            owning the pairs 256 j + 64 e + 2 l (e < 4);
-//   phase 2  one thread per channel pair: the elementwise outputs, stored with
-//            coalesced 4-byte (16-bit pair) or 8-byte (fp32 pair) stores, and
-//            the backward's per-channel sums over tokens in registers.
-// Phase 2 needs no per-channel state beyond a few registers, so the kernel runs
-// several CTAs per SM and keeps a deep ring of bytes in flight.
+//   phase 2  one thread per channel pair: the elementwise outputs, written
+//            over the staged x tile and sent out with one bulk store per tile,
+//            and the backward's per-channel sums over tokens in registers.
+// Phase 2 needs no per-channel state beyond a few registers.  Phase 1 of the
+// next tile overlaps phase 2 of the current one (one CTA barrier per tile).
 #pragma once
 
 #include "lthc_common.cuh"
@@ -115,8 +115,8 @@ struct FinalSmem {
     tile_bytes = static_cast<size_t>(tile) * C * es;
     const size_t tiles = static_cast<size_t>(stages) * (bwd ? 2 : 1) * tile_bytes;
     consts = tiles;                                    // w, 1 + scale, shift: fp32 [C] each
-    r = consts + 3 * static_cast<size_t>(C) * 4;       // r, grad of the squares: fp32 [tile] each
-    bars = (r + 2 * static_cast<size_t>(tile) * 4 + 7) & ~static_cast<size_t>(7);
+    r = consts + 3 * static_cast<size_t>(C) * 4;       // r, grad of the squares: fp32 [2][tile] each
+    bars = (r + 4 * static_cast<size_t>(tile) * 4 + 7) & ~static_cast<size_t>(7);
     total = bars + static_cast<size_t>(stages) * 8;
   }
 };
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
   float* sh_s = w_s + C;
   T* s1_s = reinterpret_cast<T*>(sh_s + C);  // 1 + scale, rounded to the dtype
   float* r_s = reinterpret_cast<float*>(smem + plan.r);
-  float* gsq_s = r_s + p.tile;
+  float* gsq_s = r_s + 2 * p.tile;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bars);
 
   const int64_t b = blockIdx.y;
@@ -197,8 +197,9 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
     bulk_load_1d(smem + (s * NT) * plan.tile_bytes, xg + off, bytes, &full[s]);
     if constexpr (BWD) bulk_load_1d(smem + (s * NT + 1) * plan.tile_bytes, gg + off, bytes, &full[s]);
   };
+  int issued = 0;  // thread 0: tiles whose copies have been started
   if (tid == 0)
-    for (int i = 0; i < min(p.stages, n_tiles); ++i) issue(i);
+    for (; issued < min(p.stages, n_tiles); ++issued) issue(issued);
 
   // Phase-2 ownership: channel pair (c, c + 1), c = 2 * tid.
   const int64_t c = 2 * static_cast<int64_t>(tid);
@@ -209,16 +210,21 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
   const float2 two = make_float2(2.f, 2.f);
   float2 aw = make_float2(0.f, 0.f), ash = aw, asc = aw;
 
-  for (int i = 0; i < n_tiles; ++i) {
-    const int s = i % p.stages;
-    const bool ok = mbar_wait(&full[s], (i / p.stages) & 1);
-    if (!__syncthreads_and(ok)) break;
+  auto tile_rows = [&](int i) -> int {
     const int64_t left = ntok - static_cast<int64_t>(i) * p.tile;
-    const int n = static_cast<int>(left < p.tile ? left : p.tile);
-    const T* xs = reinterpret_cast<const T*>(smem + (s * NT) * plan.tile_bytes);
-    const T* gs = reinterpret_cast<const T*>(smem + (s * NT + 1) * plan.tile_bytes);
+    return static_cast<int>(left < p.tile ? left : p.tile);
+  };
+  auto stage_x = [&](int i) { return reinterpret_cast<const T*>(smem + ((i % p.stages) * NT) * plan.tile_bytes); };
+  auto stage_g = [&](int i) { return reinterpret_cast<const T*>(smem + ((i % p.stages) * NT + 1) * plan.tile_bytes); };
 
-    // ---- phase 1: per-token sums (warp per token) ----
+  // Phase 1 of tile i: per-token sums (warp per token) into r / grad-of-squares
+  // buffer i & 1.
+  auto phase1 = [&](int i) {
+    const int n = tile_rows(i);
+    const T* xs = stage_x(i);
+    const T* gs = stage_g(i);
+    float* rb = r_s + (i & 1) * p.tile;
+    float* qb = gsq_s + (i & 1) * p.tile;
     for (int k = warp; k < n; k += nwarps) {
       float2 v[NV][4];
 #pragma unroll
@@ -251,39 +257,81 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
         gsq = __fdiv_rn(gv, p.c_f);
       }
       if (lane == 0) {
-        r_s[k] = r;
-        gsq_s[k] = gsq;
+        rb[k] = r;
+        qb[k] = gsq;
       }
+    }
+  };
+
+  // Phase 2 of tile i: elementwise outputs (thread per channel pair).
+  auto phase2 = [&](int i) {
+    if (!own) return;
+    const int n = tile_rows(i);
+    const T* xs = stage_x(i);
+    const T* gs = stage_g(i);
+    const float* rb = r_s + (i & 1) * p.tile;
+    const float* qb = gsq_s + (i & 1) * p.tile;
+#pragma unroll 2
+    for (int k = 0; k < n; ++k) {
+      const float2 xv = P2::f(ld_pair<T>(xs + k * C + c));
+      const float r = rb[k];
+      const float2 tt = fmul2(xv, make_float2(r, r));
+      const R nr = P2::rn(fmul2(tt, wv));  // n, rounded to the dtype
+      R* dst = reinterpret_cast<R*>(const_cast<T*>(xs) + k * C + c);  // result over x, stored by bulk copy
+      if constexpr (!BWD) {
+        *dst = P2::rn(fadd2(P2::f(P2::mul(nr, s1r)), shv));
+      } else {
+        const R gr = ld_pair<T>(gs + k * C + c);
+        const float2 gm = P2::f(gr);
+        const float gsq = qb[k];
+        const float2 gn = P2::f(P2::mul(gr, s1r));
+        ash = fadd2(ash, gm);
+        asc = fadd2(asc, P2::f(P2::mul(gr, nr)));
+        aw = fadd2(aw, fmul2(gn, tt));
+        const float2 gt = fmul2(gn, wv);
+        *dst = P2::rn(fadd2(fmul2(gt, make_float2(r, r)), fmul2(make_float2(gsq, gsq), fmul2(two, xv))));
+      }
+    }
+    fence_proxy_async_smem();  // the tile's bulk store reads these writes
+  };
+
+  // Software pipeline, one CTA barrier per tile: phase 2 of tile i runs while
+  // other warps already do phase 1 of tile i + 1; the barrier then publishes
+  // tile i's results (stored by thread 0) and tile i + 1's sums.
+  bool alive = n_tiles > 0;
+  int done = 0;  // tiles whose copies every thread has waited for
+  if (alive) {
+    alive = __syncthreads_and(mbar_wait(&full[0], 0));
+    if (alive) {
+      done = 1;
+      phase1(0);
     }
     __syncthreads();
-
-    // ---- phase 2: elementwise outputs (thread per channel pair) ----
-    if (own) {
-      const int64_t tok0 = static_cast<int64_t>(i) * p.tile;
-#pragma unroll 2
-      for (int k = 0; k < n; ++k) {
-        const float2 xv = P2::f(ld_pair<T>(xs + k * C + c));
-        const float r = r_s[k];
-        const float2 tt = fmul2(xv, make_float2(r, r));
-        const R nr = P2::rn(fmul2(tt, wv));  // n, rounded to the dtype
-        R* dst = reinterpret_cast<R*>(og + (tok0 + k) * C + c);
-        if constexpr (!BWD) {
-          *dst = P2::rn(fadd2(P2::f(P2::mul(nr, s1r)), shv));
-        } else {
-          const R gr = ld_pair<T>(gs + k * C + c);
-          const float2 gm = P2::f(gr);
-          const float gsq = gsq_s[k];
-          const float2 gn = P2::f(P2::mul(gr, s1r));
-          ash = fadd2(ash, gm);
-          asc = fadd2(asc, P2::f(P2::mul(gr, nr)));
-          aw = fadd2(aw, fmul2(gn, tt));
-          const float2 gt = fmul2(gn, wv);
-          *dst = P2::rn(fadd2(fmul2(gt, make_float2(r, r)), fmul2(make_float2(gsq, gsq), fmul2(two, xv))));
-        }
-      }
+  }
+  for (int i = 0; alive && i < n_tiles; ++i) {
+    phase2(i);
+    bool ok = true;
+    if (i + 1 < n_tiles) {
+      ok = mbar_wait(&full[(i + 1) % p.stages], ((i + 1) / p.stages) & 1);
+      if (ok) phase1(i + 1);
     }
-    __syncthreads();  // stage s consumed
-    if (tid == 0 && i + p.stages < n_tiles) issue(i + p.stages);
+    alive = __syncthreads_and(ok);
+    if (alive && i + 1 < n_tiles) done = i + 2;
+    if (tid == 0 && alive) {
+      // Tile i's results leave with one bulk store; the stage of tile i - 1 is
+      // refilled once its store has read it (one store of lag).
+      bulk_store_1d(og + static_cast<int64_t>(i) * p.tile * C, stage_x(i),
+                    static_cast<uint32_t>(tile_rows(i) * C * kEs));
+      bulk_commit();
+      bulk_wait_read<1>();
+      if (i >= 1 && i - 1 + p.stages < n_tiles) issue(issued++);
+    }
+  }
+  if (tid == 0) {
+    // a wait gave up: do not leave while copies into this CTA's memory are in flight
+    for (int i = done; i < issued; ++i)
+      if (!mbar_wait(&full[i % p.stages], (i / p.stages) & 1)) break;
+    bulk_wait_all();
   }
   if constexpr (BWD) {
     if (own) {

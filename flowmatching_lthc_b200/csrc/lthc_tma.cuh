@@ -138,6 +138,14 @@ __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_
                : "memory");
 }
 
+// Untiled bulk copy shared -> global of `bytes` contiguous bytes (16-byte aligned
+// addresses, size a multiple of 16), tracked by the bulk-group commit / wait.
+__device__ __forceinline__ void bulk_store_1d(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
 // TMA tile stores (shared -> global).  Elements outside the tensor are not
 // written, so a box that overhangs the residual or the last channel slice is
 // clipped by the hardware.

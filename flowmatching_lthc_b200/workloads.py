@@ -117,3 +117,15 @@ def read_bwd_bytes(B: int, G: int, C: int, act_bytes: int, w_bytes: int) -> int:
 
 def lazy_bytes(N: int, C: int, act_bytes: int, w_bytes: int) -> int:
     return 3 * N * C * act_bytes + 2 * C * 16 * w_bytes
+
+
+def final_fwd_bytes(B: int, T: int, C: int, act_bytes: int, w_bytes: int = 4) -> int:
+    """Final-layer norm + modulate: read x, write m, read the norm weight and the
+    image's shift / scale rows (805,318,656 + ... B at B = 64, T = 4096, C = 768)."""
+    return 2 * B * T * C * act_bytes + C * w_bytes + 2 * B * C * act_bytes
+
+
+def final_bwd_bytes(B: int, T: int, C: int, act_bytes: int, w_bytes: int = 4) -> int:
+    """Its backward: read x and grad m, write grad x; weight, scale rows and the
+    fp32 weight / shift / scale gradients are small."""
+    return 3 * B * T * C * act_bytes + C * w_bytes + B * C * act_bytes + (C + 2 * B * C) * 4
