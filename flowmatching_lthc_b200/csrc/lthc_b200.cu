@@ -19,6 +19,7 @@
 #include "lthc_broadcast_tma.cuh"
 #include "lthc_pool_tma.cuh"
 #include "lthc_final.cuh"
+#include "lthc_umma.cuh"
 
 namespace lthc {
 
@@ -586,6 +587,20 @@ int lthc_selftest_wait_timeout(int limit_ms, int* result_dev, void* stream) {
   wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<unsigned long long>(limit_ms) * 1000000ull, result_dev);
   return launched("wait-timeout self-test");
+}
+
+int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int* status_dev, void* stream) {
+  if (!A || !B || !D || !status_dev) return fail(LTHC_ERR_NULL_POINTER, "A, B, D and status must be set");
+  if (!(N == 64 || N == 128 || N == 256)) return fail(LTHC_ERR_SHAPE, "N must be 64, 128 or 256, got %d", N);
+  if (K < 64 || K > 256 || K % 64) return fail(LTHC_ERR_SHAPE, "K must be 64, 128, 192 or 256, got %d", K);
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  const int smem = 1024 + (K / 64) * (128 + N) * 128 + 16;
+  int per_sm = 0;
+  LTHC_TRY(resident_ctas(umma_selftest_kernel, 128, smem, &per_sm));
+  umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B), D, N, K, status_dev);
+  return launched("tcgen05 self-test");
 }
 
 // ------------------------------ write family ---------------------------------

@@ -216,6 +216,14 @@ LTHC_API int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const 
                          size_t workspace_bytes, int64_t N, int64_t C, int act_dtype,
                          void* stream);
 
+/* Tensor-core self-test: D[128 x N] = A[128 x K] * B[N x K]^T with A, B row-major
+ * bf16 and D fp32 on the 5th-generation tensor cores (tcgen05, TMEM), one CTA.
+ * N in {64, 128, 256}; K in {64, 128, 192, 256}.  *status_dev receives 0, or 1
+ * if the bounded wait for the MMA gave up.  Validates the operand descriptors
+ * used by the tensor-core kernels of this library. */
+LTHC_API int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int* status_dev,
+                         void* stream);
+
 /* ======================= final-layer prologue on the residual =============== */
 
 /* m[b,t,:] = modulate(RMSNorm(x[b,t,:]), shift[b,:], scale[b,:]) over the
