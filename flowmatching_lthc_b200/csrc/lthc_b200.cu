@@ -20,6 +20,7 @@
 #include "lthc_pool_tma.cuh"
 #include "lthc_final.cuh"
 #include "lthc_umma.cuh"
+#include "lthc_embed.cuh"
 
 namespace lthc {
 
@@ -411,6 +412,26 @@ int read_family(const ReadJob& j, size_t ws_bytes, int act, cudaStream_t s) {
 
 int check_weight_dtype(int dt, const char* name) {
   if (!valid_act(dt)) return fail(LTHC_ERR_DTYPE, "unknown %s dtype code %d", name, dt);
+  return LTHC_OK;
+}
+
+// ---- patch embedding fused with the shared read (tensor cores) -----------------
+
+// X0 NHWC [B, H, H, C] bf16 as a 4-D map (C, W, H, B) for the staged tile stores:
+// box = 64 channels x 32 columns x 4 rows, 128-byte swizzle (the UMMA operand
+// layout of the staging buffer).
+int encode_embed_store_map(CUtensorMap* m, void* ptr, int64_t B, int64_t H, int64_t C) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(LTHC_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t es = 2;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {C * es, H * C * es, H * H * C * es};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(kEmbedTileCols), 4, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (embed store) failed with %d", (int)r);
   return LTHC_OK;
 }
 
@@ -905,6 +926,56 @@ int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alp
     LTHC_TRY(launched("lazy update backward finalize"));
   }
   return LTHC_OK;
+}
+
+// ------------------- patch embedding fused with the shared read ----------------
+
+int lthc_patch_embed_read_fwd(const void* img, int img_dtype, const void* w1, const void* w2, const void* b2,
+                              const void* alpha, void* x0, void* z, int64_t B, int in_ch, int64_t H, int64_t C,
+                              void* stream) {
+  if (B < 0 || B > 65535) return fail(LTHC_ERR_SHAPE, "batch must be in [0, 65535], got %lld", (long long)B);
+  if (in_ch < 1 || in_ch > 4) return fail(LTHC_ERR_SHAPE, "input channels must be in [1, 4], got %d", in_ch);
+  if (H < kEmbedTileCols || H % kEmbedTileCols || H > 1024)
+    return fail(LTHC_ERR_SHAPE, "token grid side must be a multiple of %d in [%d, 1024], got %lld", kEmbedTileCols,
+                kEmbedTileCols, (long long)H);
+  if (C < kEmbedChunk || C % kEmbedChunk || C > 4096)
+    return fail(LTHC_ERR_SHAPE, "embed channels must be a multiple of %d in [%d, 4096], got %lld", kEmbedChunk,
+                kEmbedChunk, (long long)C);
+  if (img_dtype != LTHC_DTYPE_F32 && img_dtype != LTHC_DTYPE_BF16)
+    return fail(LTHC_ERR_DTYPE, "image dtype must be fp32 or bf16, got code %d", img_dtype);
+  const bool nonempty = B > 0;
+  LTHC_TRY(check_act(img, "img", nonempty));
+  LTHC_TRY(check_act(x0, "x0", nonempty));
+  LTHC_TRY(check_act(z, "z", nonempty));
+  LTHC_TRY(check_ptr(w1, "w1"));
+  LTHC_TRY(check_ptr(w2, "w2"));
+  LTHC_TRY(check_ptr(b2, "b2"));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  if (!nonempty) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  EmbedParams p;
+  memset(&p, 0, sizeof(p));
+  LTHC_TRY(encode_embed_store_map(&p.tm_x0, x0, B, H, C));
+  p.img = img;
+  p.w1 = static_cast<const __nv_bfloat16*>(w1);
+  p.w2 = static_cast<const __nv_bfloat16*>(w2);
+  p.b2 = static_cast<const __nv_bfloat16*>(b2);
+  p.alpha = static_cast<const __nv_bfloat16*>(alpha);
+  p.z = static_cast<__nv_bfloat16*>(z);
+  p.img_f32 = img_dtype == LTHC_DTYPE_F32;
+  p.in_ch = in_ch;
+  p.H = static_cast<int>(H);
+  p.C = static_cast<int>(C);
+  p.B = B;
+  p.tiles = B * (H / 4) * (H / kEmbedTileCols);
+  const int nchunks = static_cast<int>(C / kEmbedChunk);
+  int per_sm = 0;
+  LTHC_TRY(resident_ctas(patch_embed_read_kernel, kEmbedThreads, static_cast<int>(EmbedSmem::kTotal), &per_sm));
+  const int64_t per_chunk = std::max<int64_t>(1, std::min<int64_t>(sms / nchunks, p.tiles));
+  const unsigned grid = static_cast<unsigned>(per_chunk * nchunks);
+  patch_embed_read_kernel<<<grid, kEmbedThreads, EmbedSmem::kTotal, static_cast<cudaStream_t>(stream)>>>(p);
+  return launched("patch embedding + read (tensor cores)");
 }
 
 // ------------------------- final-layer prologue --------------------------------

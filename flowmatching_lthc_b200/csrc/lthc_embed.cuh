@@ -1,0 +1,284 @@
+// Patch embedding fused with the shared read, on the tensor cores (row (f)2 of
+// the LTHC path):
+//   h1 = conv4x4/4(img; W1)        [tokens, 128]   (BottleneckPatchEmbedNHWC.proj1)
+//   X0 = conv1x1(h1; W2) + b2      [tokens, C]     (proj2, then NHWC)
+//   Z  = R(X0)                     [cells, C]      (SharedLocalRead.read)
+// (local_thc.py:64-89 and 1211-1223).  Under bf16 autocast the reference runs
+// both convolutions in bf16 with fp32 accumulation (h1 and the second product
+// rounded to bf16, the bias then added as a separate bf16 op), writes X0 in NCHW,
+// permutes it to NHWC and reads X0 back for Z.  This kernel rounds the same way
+// (measured on B200: h1 identical to cuDNN's, X0 more than 99.99 %).  Here
+// one pass computes both GEMMs per tile of 128 tokens with tcgen05 MMAs
+// (accumulators in TMEM), writes X0 once (TMA tile stores) and pools Z from the
+// staged X0 tile, in the same fp32 fused-multiply-add order as lthc_read_fwd, so
+// Z equals the read of the X0 this kernel writes bit for bit.
+//
+// Tile: one image, one cell row, 8 cells = 4 token rows x 32 token columns; MMA
+// row m = 16 * cell + 4 * row + col (a cell's 16 tokens are consecutive TMEM
+// lanes).  A CTA owns one 256-channel chunk of X0 (its W2 rows stay in shared
+// memory) and walks tiles; h1 is recomputed for each chunk (K = 48, cheap).
+//
+//   GEMM 1: D1[128 x 128] = A1[128 x 48(+16 zero)] * W1[128 x 48]^T     (3 K steps)
+//   GEMM 2: D2[128 x 256] = A2[128 x 128] * W2chunk[256 x 128]^T      (8 K steps)
+// Operands are K-major, 128-byte-swizzled bf16 (lthc_umma.cuh).
+#pragma once
+
+#include "lthc_common.cuh"
+#include "lthc_tma.cuh"
+#include "lthc_umma.cuh"
+
+namespace lthc {
+
+// (a, b) rounded to bf16 and widened back to fp32.
+__device__ __forceinline__ float2 bf16_round2(float a, float b) {
+  const __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return __bfloat1622float2(t);
+}
+
+constexpr int kEmbedThreads = 256;     // 8 warps; two per TMEM lane quarter
+constexpr int kEmbedTileTokens = 128;  // MMA M
+constexpr int kEmbedBottleneck = 128;  // GEMM-1 N = GEMM-2 K
+constexpr int kEmbedChunk = 256;       // GEMM-2 N: X0 channels per CTA
+constexpr int kEmbedTileCols = 32;     // token columns per tile (8 cells)
+
+struct EmbedParams {
+  CUtensorMap tm_x0;        // 4D (C, W, H, B) bf16, box (64, 32, 4, 1), 128-byte swizzle (store)
+  const void* img;          // [B, in_ch, 4H, 4W] fp32 or bf16
+  const __nv_bfloat16* w1;  // [128, in_ch * 16]
+  const __nv_bfloat16* w2;  // [C, 128]
+  const __nv_bfloat16* b2;  // [C]
+  const __nv_bfloat16* alpha;  // [C, 16] read weights (activation dtype)
+  __nv_bfloat16* z;         // [B, (H/4)*(W/4), C]
+  int img_f32;
+  int in_ch;
+  int H;                    // token grid side (64 at B/4)
+  int C;
+  int64_t B;
+  int64_t tiles;            // B * (H/4) * (W/32)
+};
+
+// Shared-memory plan (offsets from a 1024-byte aligned base).
+struct EmbedSmem {
+  static constexpr uint32_t kW1 = 0;                                      // 128 x 64  : 16 KB
+  static constexpr uint32_t kW2 = kW1 + 16384;                            // 2 x 256 x 64 : 64 KB
+  static constexpr uint32_t kA1 = kW2 + 65536;                            // 128 x 64 : 16 KB
+  static constexpr uint32_t kA2 = kA1 + 16384;                            // 2 x 128 x 64 : 32 KB
+  static constexpr uint32_t kX = kA2 + 32768;                             // 4 x 128 x 64 : 64 KB
+  static constexpr uint32_t kAlpha = kX + 65536;                          // fp32 [16][256] : 16 KB
+  static constexpr uint32_t kBias = kAlpha + 16384;                       // fp32 [256]
+  static constexpr uint32_t kBars = kBias + 1024;                         // 2 mbarriers + TMEM slot
+  static constexpr uint32_t kTotal = kBars + 64 + 1024;                   // + alignment slack
+};
+constexpr uint32_t kEmbedTmemCols = 512;  // D1: columns [0, 128); D2: [128, 384)
+
+__global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(const __grid_constant__ EmbedParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar1 = reinterpret_cast<uint64_t*>(smem + EmbedSmem::kBars);
+  uint64_t* bar2 = bar1 + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar1 + 2);
+  float* alpha_s = reinterpret_cast<float*>(smem + EmbedSmem::kAlpha);
+  float* bias_s = reinterpret_cast<float*>(smem + EmbedSmem::kBias);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nchunks = p.C / kEmbedChunk;
+  const int chunk = blockIdx.x % nchunks;
+  const int cta_in_chunk = blockIdx.x / nchunks;
+  const int ctas_per_chunk = gridDim.x / nchunks;
+  const int n0 = chunk * kEmbedChunk;
+  const int K1 = p.in_ch * 16;
+
+  // ---- one-time set-up: weights, read weights, bias; zero the GEMM-1 K padding
+  for (int i = tid; i < 128 * 64; i += kEmbedThreads) {
+    const int r = i >> 6, k = i & 63;
+    const __nv_bfloat16 v = k < K1 ? p.w1[r * K1 + k] : __float2bfloat16_rn(0.f);
+    *reinterpret_cast<__nv_bfloat16*>(smem + EmbedSmem::kW1 + sw128_offset(r, k)) = v;
+    *reinterpret_cast<__nv_bfloat16*>(smem + EmbedSmem::kA1 + sw128_offset(r, k)) = __float2bfloat16_rn(0.f);
+  }
+  for (int i = tid; i < kEmbedChunk * kEmbedBottleneck / 8; i += kEmbedThreads) {
+    const int r = i / (kEmbedBottleneck / 8), k8 = (i % (kEmbedBottleneck / 8)) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(p.w2 + static_cast<int64_t>(n0 + r) * kEmbedBottleneck + k8);
+    *reinterpret_cast<uint4*>(smem + EmbedSmem::kW2 + (k8 >> 6) * 32768 + sw128_offset(r, k8 & 63)) = v;
+  }
+  for (int i = tid; i < kEmbedChunk * 16; i += kEmbedThreads) {
+    const int n = i >> 4, r = i & 15;
+    alpha_s[r * kEmbedChunk + n] = __bfloat162float(p.alpha[static_cast<int64_t>(n0 + n) * 16 + r]);
+  }
+  for (int n = tid; n < kEmbedChunk; n += kEmbedThreads) bias_s[n] = __bfloat162float(p.b2[n0 + n]);
+  if (tid == 0) {
+    mbar_init(bar1, 1);
+    mbar_init(bar2, 1);
+    fence_barrier_init();
+    prefetch_tmap(&p.tm_x0);
+  }
+  if (warp == 0) tmem_alloc(tslot, kEmbedTmemCols);
+  fence_proxy_async_smem();
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t tmem_d1 = tmem;
+  const uint32_t tmem_d2 = tmem + kEmbedBottleneck;
+  const uint32_t idesc1 = umma_idesc_bf16_f32(kEmbedTileTokens, kEmbedBottleneck);
+  const uint32_t idesc2 = umma_idesc_bf16_f32(kEmbedTileTokens, kEmbedChunk);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int cell_rows = p.H / 4;
+  const int halves = p.H / kEmbedTileCols;
+  const int lq = warp & 3;            // TMEM lane quarter of this warp
+  const int hf = warp >> 2;           // column half handled by this warp
+  const int m = 32 * lq + lane;       // this thread's MMA row (token of the tile)
+  const int m_cell = m >> 4, m_r = m & 15;
+  const int m_R = (m_r >> 2) * kEmbedTileCols + 4 * m_cell + (m_r & 3);  // row of the staged X0 box
+  const int64_t img_w = 4 * static_cast<int64_t>(p.H);
+  bool alive = true;
+  int it = 0;
+
+  for (int64_t tile = cta_in_chunk; alive && tile < p.tiles; tile += ctas_per_chunk, ++it) {
+    const int64_t b = tile / (cell_rows * halves);
+    const int rem = static_cast<int>(tile - b * cell_rows * halves);
+    const int wy = rem / halves, hx = rem % halves;
+
+    // ---- A1: gather the tile's patches (4 pixels = one token, one channel, one kernel row per load)
+    const int per_tile = p.in_ch * 16 * (kEmbedTileCols);  // loads of 4 pixels
+    for (int i = tid; i < per_tile; i += kEmbedThreads) {
+      const int tx = i % kEmbedTileCols;           // token column in the tile
+      const int py = (i / kEmbedTileCols) % 16;    // pixel row in the tile
+      const int c = i / (kEmbedTileCols * 16);
+      const int64_t gy = 16 * static_cast<int64_t>(wy) + py;
+      const int64_t gx = 4 * (static_cast<int64_t>(kEmbedTileCols) * hx + tx);
+      const int64_t off = ((b * p.in_ch + c) * img_w + gy) * img_w + gx;
+      uint2 packed;
+      if (p.img_f32) {
+        const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(p.img) + off);
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        packed.x = *reinterpret_cast<uint32_t*>(&lo);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi);
+      } else {
+        packed = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.img) + off);
+      }
+      const int row = py >> 2, ky = py & 3;
+      const int mm = 16 * (tx >> 2) + 4 * row + (tx & 3);
+      const int k = c * 16 + ky * 4;
+      *reinterpret_cast<uint2*>(smem + EmbedSmem::kA1 + sw128_offset(mm, k)) = packed;
+    }
+    fence_proxy_async_smem();
+    tmem_fence_before_sync();
+    __syncthreads();
+
+    // ---- GEMM 1
+    if (tid == 0) {
+      tmem_fence_after_sync();
+      for (int s = 0; s < p.in_ch; ++s)
+        umma_bf16(tmem_d1, umma_desc_sw128(sbase + EmbedSmem::kA1 + 32 * s),
+                  umma_desc_sw128(sbase + EmbedSmem::kW1 + 32 * s), idesc1, s > 0);
+      umma_commit(bar1);
+    }
+    bool ok = mbar_wait(bar1, it & 1);
+    tmem_fence_after_sync();
+
+    // ---- epilogue 1: h1 = bf16(D1) into A2 (row m, columns 64 * hf .. + 64)
+    if (ok) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float v[32];
+        tmem_ld32(tmem_d1 + (static_cast<uint32_t>(32 * lq) << 16) + 64 * hf + 32 * half, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+          __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+          __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+          __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+          w.x = *reinterpret_cast<uint32_t*>(&t0);
+          w.y = *reinterpret_cast<uint32_t*>(&t1);
+          w.z = *reinterpret_cast<uint32_t*>(&t2);
+          w.w = *reinterpret_cast<uint32_t*>(&t3);
+          *reinterpret_cast<uint4*>(smem + EmbedSmem::kA2 + hf * 16384 + sw128_offset(m, 32 * half + 8 * q)) = w;
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tmem_fence_before_sync();
+    if (tid == 0) bulk_wait_read<0>();  // the previous tile's X0 stores have read the staging buffer
+    alive = __syncthreads_and(ok);
+    if (!alive) break;
+
+    // ---- GEMM 2
+    if (tid == 0) {
+      tmem_fence_after_sync();
+      for (int s = 0; s < kEmbedBottleneck / 16; ++s)
+        umma_bf16(tmem_d2, umma_desc_sw128(sbase + EmbedSmem::kA2 + (s >> 2) * 16384 + 32 * (s & 3)),
+                  umma_desc_sw128(sbase + EmbedSmem::kW2 + (s >> 2) * 32768 + 32 * (s & 3)), idesc2, s > 0);
+      umma_commit(bar2);
+    }
+    ok = mbar_wait(bar2, it & 1);
+    tmem_fence_after_sync();
+
+    // ---- epilogue 2: X0 = bf16(D2 + b2) into the staging boxes (row m_R, channels 128 * hf .. + 128)
+    if (ok) {
+#pragma unroll
+      for (int q32 = 0; q32 < 4; ++q32) {
+        float v[32];
+        const int nb = 128 * hf + 32 * q32;  // first channel of these 32 within the chunk
+        tmem_ld32(tmem_d2 + (static_cast<uint32_t>(32 * lq) << 16) + nb, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int n = nb + 8 * q;
+          // the convolution output is rounded to bf16, then the bias is added and
+          // the sum rounded again (the reference adds the bias as a separate op)
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 conv = bf16_round2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+            const __nv_bfloat162 t =
+                __floats2bfloat162_rn(__fadd_rn(conv.x, bias_s[n + 2 * e]), __fadd_rn(conv.y, bias_s[n + 2 * e + 1]));
+            o[e] = *reinterpret_cast<const uint32_t*>(&t);
+          }
+          uint4 w;
+          w.x = o[0];
+          w.y = o[1];
+          w.z = o[2];
+          w.w = o[3];
+          *reinterpret_cast<uint4*>(smem + EmbedSmem::kX + (n >> 6) * 16384 + sw128_offset(m_R, n & 63)) = w;
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tmem_fence_before_sync();
+    alive = __syncthreads_and(ok);
+    if (!alive) break;
+
+    // ---- X0 out: four TMA tile stores of 64 channels x 32 columns x 4 rows
+    if (tid == 0) {
+#pragma unroll
+      for (int bx = 0; bx < kEmbedChunk / 64; ++bx)
+        tma_store_4d(&p.tm_x0, smem + EmbedSmem::kX + bx * 16384, n0 + 64 * bx, kEmbedTileCols * hx, 4 * wy,
+                     static_cast<int32_t>(b));
+      bulk_commit();
+    }
+
+    // ---- Z: pool the staged X0 over each cell's 16 positions (r = 0..15 in order, fp32 FMA)
+    const int64_t zrow0 = b * static_cast<int64_t>(cell_rows) * (p.H / 4) + static_cast<int64_t>(wy) * (p.H / 4) +
+                          (kEmbedTileCols / 4) * hx;
+    for (int pi = tid; pi < 8 * (kEmbedChunk / 2); pi += kEmbedThreads) {
+      const int cell = pi / (kEmbedChunk / 2);
+      const int n = 2 * (pi % (kEmbedChunk / 2));
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int R = (r >> 2) * kEmbedTileCols + 4 * cell + (r & 3);
+        const uint32_t raw =
+            *reinterpret_cast<const uint32_t*>(smem + EmbedSmem::kX + (n >> 6) * 16384 + sw128_offset(R, n & 63));
+        const float2 a = *reinterpret_cast<const float2*>(alpha_s + r * kEmbedChunk + n);
+        acc = ffma2(a, Act<__nv_bfloat16>::cvt(raw), acc);
+      }
+      Act<__nv_bfloat16>::st(p.z + (zrow0 + cell) * p.C + n0 + n, acc);
+    }
+  }
+  if (tid == 0) bulk_wait_all();
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kEmbedTmemCols);
+}
+
+}  // namespace lthc

@@ -475,6 +475,103 @@ def _(high, low):
 
 
 # ---------------------------------------------------------------------------
+# patch embedding fused with the shared read (tensor cores)
+# (BottleneckPatchEmbedNHWC.forward, local_thc.py:64-89, then SharedLocalRead.read,
+# :1211-1223)
+# ---------------------------------------------------------------------------
+EMBED_CHUNK = 256
+EMBED_TILE_COLS = 32
+
+
+def embed_supported(img: Tensor, w1: Tensor, w2: Tensor) -> bool:
+    """Shapes the fused kernel takes: 4x4/4 patches of 1..4 channels into a 128-wide
+    bottleneck, C a multiple of 256, a token grid side that is a multiple of 32."""
+    if img.dim() != 4 or w1.dim() != 4 or w2.dim() != 4:
+        return False
+    b, cin, s, s2 = img.shape
+    return (s == s2 and s % (4 * EMBED_TILE_COLS) == 0 and tuple(w1.shape) == (128, cin, 4, 4) and 1 <= cin <= 4
+            and w2.shape[1] == 128 and tuple(w2.shape[2:]) == (1, 1) and w2.shape[0] % EMBED_CHUNK == 0)
+
+
+@torch.library.custom_op("lthc_b200::patch_embed_read", mutates_args=(), device_types="cuda")
+def patch_embed_read(img: Tensor, w1: Tensor, w2: Tensor, b2: Tensor, alpha: Tensor) -> tuple[Tensor, Tensor]:
+    """(X0 [B,H,H,C] bf16, Z [B,(H/4)^2,C] bf16): both convolutions in bf16 with fp32
+    accumulation on the tensor cores, then the read of X0 with alpha."""
+    _require_cuda(img, w1, w2, b2, alpha)
+    if not embed_supported(img, w1, w2):
+        raise ValueError(f"patch_embed_read: unsupported shapes img {tuple(img.shape)}, w1 {tuple(w1.shape)}, "
+                         f"w2 {tuple(w2.shape)}")
+    b, cin, s, _ = img.shape
+    c = w2.shape[0]
+    h = s // 4
+    if tuple(b2.shape) != (c,) or tuple(alpha.shape) != (c, 16):
+        raise ValueError(f"patch_embed_read: expected bias [{c}] and alpha [{c},16]")
+    if img.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"patch_embed_read: image dtype {img.dtype} (float32 or bfloat16)")
+    bf = torch.bfloat16
+    img = img.contiguous()
+    w1b = w1.to(bf).reshape(128, cin * 16).contiguous()
+    w2b = w2.to(bf).reshape(c, 128).contiguous()
+    b2b, ab = b2.to(bf).contiguous(), alpha.to(bf).contiguous()
+    x0 = torch.empty((b, h, h, c), device=img.device, dtype=bf)
+    z = torch.empty((b, (h // 4) ** 2, c), device=img.device, dtype=bf)
+    with _guard(img):
+        _lib.call("lthc_patch_embed_read_fwd", img.data_ptr(), _code(img, "patch_embed_read"), w1b.data_ptr(),
+                  w2b.data_ptr(), b2b.data_ptr(), ab.data_ptr(), x0.data_ptr(), z.data_ptr(), b, cin, h, c,
+                  _stream(img))
+    return x0, z
+
+
+@patch_embed_read.register_fake
+def _(img, w1, w2, b2, alpha):
+    b, _, s, _ = img.shape
+    c, h = w2.shape[0], s // 4
+    bf = torch.bfloat16
+    return img.new_empty((b, h, h, c), dtype=bf), img.new_empty((b, (h // 4) ** 2, c), dtype=bf)
+
+
+def _embed_setup(ctx, inputs, output):
+    img, w1, w2, b2, alpha = inputs
+    x0, _ = output
+    ctx.save_for_backward(img, w1, w2, alpha, x0)
+    ctx.b2_dtype = b2.dtype
+
+
+def _embed_backward(ctx, g_x0, g_z):
+    """Read backward (lthc_read_bwd) into grad X0, then the two convolutions'
+    backward as library GEMMs on the bf16 operands (h1 recomputed)."""
+    img, w1, w2, alpha, x0 = ctx.saved_tensors
+    need_img, need_w1, need_w2, need_b2, need_a = ctx.needs_input_grad
+    bf = torch.bfloat16
+    b, cin, s, _ = img.shape
+    c, h = w2.shape[0], s // 4
+    gx = g_x0 if g_x0 is not None else torch.zeros_like(x0)
+    ga = None
+    if g_z is not None:
+        gxr, ga = read_bwd(x0, g_z.to(bf), alpha.to(bf), True, need_a)
+        gx = gx.to(bf) + gxr
+    g2 = gx.to(bf).reshape(-1, c)                                              # [tokens, C]
+    patches = (img.to(bf).reshape(b, cin, h, 4, h, 4).permute(0, 2, 4, 1, 3, 5).reshape(-1, cin * 16))
+    w1b = w1.to(bf).reshape(128, cin * 16)
+    w2b = w2.to(bf).reshape(c, 128)
+    h1 = patches @ w1b.t()                                                     # [tokens, 128] bf16
+    gw2 = (g2.t() @ h1).reshape(w2.shape).to(w2.dtype) if need_w2 else None
+    gb2 = g2.float().sum(0).to(ctx.b2_dtype) if need_b2 else None
+    gw1 = None
+    if need_w1 or need_img:
+        gh1 = g2 @ w2b                                                         # [tokens, 128]
+        gw1 = (gh1.t() @ patches).reshape(w1.shape).to(w1.dtype) if need_w1 else None
+    gimg = None
+    if need_img:
+        gp = (gh1 @ w1b).float()                                               # [tokens, cin*16]
+        gimg = gp.reshape(b, h, h, cin, 4, 4).permute(0, 3, 1, 4, 2, 5).reshape(img.shape).to(img.dtype)
+    return gimg, gw1, gw2, gb2, (ga.to(alpha.dtype) if (need_a and ga is not None) else None)
+
+
+patch_embed_read.register_autograd(_embed_backward, setup_context=_embed_setup)
+
+
+# ---------------------------------------------------------------------------
 # final-layer prologue  m = modulate(RMSNorm(x), shift, scale)
 # (FinalLayerSharedAdaLN.forward, local_thc.py:865-873; RMSNorm,
 # jit_shared_adaln.py:20-30; modulate, local_thc.py:37-38)

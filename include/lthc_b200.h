@@ -224,6 +224,23 @@ LTHC_API int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const 
 LTHC_API int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int* status_dev,
                          void* stream);
 
+/* ======================= patch embedding fused with the shared read ========= */
+
+/* X0 = NHWC(conv1x1(conv4x4/4(img; w1); w2) + b2) and Z = read(X0; alpha) in one
+ * pass on the tensor cores (tcgen05, bf16 operands, fp32 accumulation; the
+ * bottleneck h1 and X0 rounded to bf16 as under bf16 autocast).
+ *   img   [B, in_ch, 4H, 4H] fp32 or bf16 (img_dtype), in_ch in 1..4
+ *   w1    [128, in_ch*16] bf16 (proj1 weight, flattened), w2 [C, 128] bf16,
+ *   b2    [C] bf16, alpha [C, 16] bf16 (the shared read's weights)
+ *   x0    [B, H, H, C] bf16 out;  z [B, (H/4)^2, C] bf16 out
+ * H a multiple of 32 (64 at B/4), C a multiple of 256.  Z is computed from the
+ * bf16 X0 with the arithmetic of lthc_read_fwd (equal bits).
+ * Replaces BottleneckPatchEmbedNHWC.forward (local_thc.py:64-89) followed by
+ * SharedLocalRead.read (:1211-1223), as called by forward_lazy (:1378-1379). */
+LTHC_API int lthc_patch_embed_read_fwd(const void* img, int img_dtype, const void* w1, const void* w2,
+                         const void* b2, const void* alpha, void* x0, void* z, int64_t B,
+                         int in_ch, int64_t H, int64_t C, void* stream);
+
 /* ======================= final-layer prologue on the residual =============== */
 
 /* m[b,t,:] = modulate(RMSNorm(x[b,t,:]), shift[b,:], scale[b,:]) over the
