@@ -202,6 +202,15 @@ def op_step(op: str, cfg: dict):
         "lazy_bwd": (lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 2,
                      "lazy_bwd_kernel<bf16> + lazy_bwd_finalize_kernel"),
     }
+    if op == "embed_fwd":
+        # patch embedding + shared read of BASELINE config 3's images (B, 3, 256, 256)
+        gen = torch.Generator(device=x0.device).manual_seed(11)
+        img = torch.randn(B, 3, 4 * 4 * G, 4 * 4 * G, device=x0.device, generator=gen)
+        w1 = torch.randn(128, 3, 4, 4, device=x0.device, generator=gen) * 0.14
+        w2 = torch.randn(C, 128, 1, 1, device=x0.device, generator=gen) * 0.09
+        b2 = torch.randn(C, device=x0.device, generator=gen) * 0.1
+        table["embed_fwd"] = (lambda: ops.patch_embed_read(img, w1, w2, b2, alpha), W.embed_bytes(B, 4 * G, C), 1,
+                              "patch_embed_read_kernel (tcgen05)")
     if op in ("final_fwd", "final_bwd"):
         # final-layer prologue on the materialised residual [B, 4096, 768] (FinalLayerSharedAdaLN)
         T = 16 * G * G
@@ -217,7 +226,7 @@ def op_step(op: str, cfg: dict):
 
 
 OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
-       "final_fwd", "final_bwd")
+       "final_fwd", "final_bwd", "embed_fwd")
 MODEL_OPS = ("model_fwd", "train_step", "sample")
 # Largest batch per model call for which the reference Triton materialisation's
 # 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
@@ -398,6 +407,7 @@ WORKLOADS = {
     "lazy_bwd": "lazy update bwd, config 2 shapes",
     "final_fwd": "final-layer RMSNorm + AdaLN modulate on X_L [B, 4096, 768], config 2 shapes",
     "final_bwd": "final-layer RMSNorm + modulate bwd (grad X_L, grad norm weight / shift / scale), config 2 shapes",
+    "embed_fwd": "patch embedding (4x4 conv 3->128, 1x1 conv 128->768) + shared read, config 3 images, tcgen05",
 }
 
 

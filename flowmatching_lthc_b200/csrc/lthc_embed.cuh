@@ -40,6 +40,7 @@ constexpr int kEmbedTileTokens = 128;  // MMA M
 constexpr int kEmbedBottleneck = 128;  // GEMM-1 N = GEMM-2 K
 constexpr int kEmbedChunk = 256;       // GEMM-2 N: X0 channels per CTA
 constexpr int kEmbedTileCols = 32;     // token columns per tile (8 cells)
+constexpr int kEmbedMaxLoads = 8;      // 4-pixel loads per thread per tile (in_ch <= 4)
 
 struct EmbedParams {
   CUtensorMap tm_x0;        // 4D (C, W, H, B) bf16, box (64, 32, 4, 1), 128-byte swizzle (store)
@@ -133,34 +134,57 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
   bool alive = true;
   int it = 0;
 
+  // Patch gather: 4 pixels (one token, one channel, one kernel row) per load;
+  // load i of this thread covers pixel-row group i * kEmbedThreads + tid.
+  const int per_tile = p.in_ch * 16 * kEmbedTileCols;
+  uint2 pre[kEmbedMaxLoads];  // next tile's pixels as bf16
+  auto gather_load = [&](int64_t t) {
+    const int64_t bb = t / (cell_rows * halves);
+    const int rr = static_cast<int>(t - bb * cell_rows * halves);
+    const int wy_ = rr / halves, hx_ = rr % halves;
+#pragma unroll
+    for (int j = 0; j < kEmbedMaxLoads; ++j) {
+      const int i = j * kEmbedThreads + tid;
+      if (i < per_tile) {
+        const int tx = i % kEmbedTileCols;
+        const int py = (i / kEmbedTileCols) % 16;
+        const int c = i / (kEmbedTileCols * 16);
+        const int64_t gy = 16 * static_cast<int64_t>(wy_) + py;
+        const int64_t gx = 4 * (static_cast<int64_t>(kEmbedTileCols) * hx_ + tx);
+        const int64_t off = ((bb * p.in_ch + c) * img_w + gy) * img_w + gx;
+        if (p.img_f32) {
+          const float4 v = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(p.img) + off));
+          __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+          pre[j].x = *reinterpret_cast<uint32_t*>(&lo);
+          pre[j].y = *reinterpret_cast<uint32_t*>(&hi);
+        } else {
+          pre[j] = __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.img) + off));
+        }
+      }
+    }
+  };
+  auto gather_store = [&](const uint2 (&v)[kEmbedMaxLoads]) {
+#pragma unroll
+    for (int j = 0; j < kEmbedMaxLoads; ++j) {
+      const int i = j * kEmbedThreads + tid;
+      if (i < per_tile) {
+        const int tx = i % kEmbedTileCols;
+        const int py = (i / kEmbedTileCols) % 16;
+        const int c = i / (kEmbedTileCols * 16);
+        const int mm = 16 * (tx >> 2) + 4 * (py >> 2) + (tx & 3);
+        *reinterpret_cast<uint2*>(smem + EmbedSmem::kA1 + sw128_offset(mm, c * 16 + (py & 3) * 4)) = v[j];
+      }
+    }
+  };
+  if (cta_in_chunk < p.tiles) gather_load(cta_in_chunk);
+
   for (int64_t tile = cta_in_chunk; alive && tile < p.tiles; tile += ctas_per_chunk, ++it) {
     const int64_t b = tile / (cell_rows * halves);
     const int rem = static_cast<int>(tile - b * cell_rows * halves);
     const int wy = rem / halves, hx = rem % halves;
 
-    // ---- A1: gather the tile's patches (4 pixels = one token, one channel, one kernel row per load)
-    const int per_tile = p.in_ch * 16 * (kEmbedTileCols);  // loads of 4 pixels
-    for (int i = tid; i < per_tile; i += kEmbedThreads) {
-      const int tx = i % kEmbedTileCols;           // token column in the tile
-      const int py = (i / kEmbedTileCols) % 16;    // pixel row in the tile
-      const int c = i / (kEmbedTileCols * 16);
-      const int64_t gy = 16 * static_cast<int64_t>(wy) + py;
-      const int64_t gx = 4 * (static_cast<int64_t>(kEmbedTileCols) * hx + tx);
-      const int64_t off = ((b * p.in_ch + c) * img_w + gy) * img_w + gx;
-      uint2 packed;
-      if (p.img_f32) {
-        const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(p.img) + off);
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-        packed.x = *reinterpret_cast<uint32_t*>(&lo);
-        packed.y = *reinterpret_cast<uint32_t*>(&hi);
-      } else {
-        packed = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.img) + off);
-      }
-      const int row = py >> 2, ky = py & 3;
-      const int mm = 16 * (tx >> 2) + 4 * row + (tx & 3);
-      const int k = c * 16 + ky * 4;
-      *reinterpret_cast<uint2*>(smem + EmbedSmem::kA1 + sw128_offset(mm, k)) = packed;
-    }
+    // ---- A1: the tile's patches (loaded into registers during the previous tile)
+    gather_store(pre);
     fence_proxy_async_smem();
     tmem_fence_before_sync();
     __syncthreads();
@@ -173,6 +197,7 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
                   umma_desc_sw128(sbase + EmbedSmem::kW1 + 32 * s), idesc1, s > 0);
       umma_commit(bar1);
     }
+    if (tile + ctas_per_chunk < p.tiles) gather_load(tile + ctas_per_chunk);  // overlaps the rest of this tile
     bool ok = mbar_wait(bar1, it & 1);
     tmem_fence_after_sync();
 

@@ -16,6 +16,8 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   SharedReadFusedFinalLocalTHCSharedAdaLNJiT.final_accumulate_reference   :1407-1410 (stacked op)
   SharedReadFusedFinal12LocalTHCSharedAdaLNJiT.final_accumulate_reference :1416-1420 (released op)
   FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
+  SharedReadLocalTHCSharedAdaLNJiT.forward_lazy (patch embedding + shared read
+      fused on the tensor cores under bf16 autocast)                           :1374-1388
 
 Shape checks and messages are the reference's own; the arithmetic runs in
 ``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
@@ -97,6 +99,41 @@ def _final_layer(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
 _ORIGINAL_MODULATE = None
 
 
+def _embed_and_read(model, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """X0 = x_embedder(x) and Z = shared_read.read(X0); one fused tensor-core pass
+    under bf16 autocast when the embedder is the bottleneck patch embedding the
+    kernel takes, else the two calls."""
+    emb, sr = model.x_embedder, model.shared_read
+    fused = (x.is_cuda and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+             and all(hasattr(emb, a) for a in ("proj1", "proj2", "img_size")) and emb.proj2.bias is not None
+             and emb.proj1.bias is None and tuple(x.shape[-2:]) == tuple(emb.img_size)
+             and ops.embed_supported(x, emb.proj1.weight, emb.proj2.weight)
+             and sr.high_grid == x.shape[-1] // 4 and sr.hidden_size == emb.proj2.weight.shape[0])
+    if not fused:
+        x0 = emb(x)
+        return x0, sr.read(x0)
+    c = emb.proj2.weight.shape[0]
+    alpha = per_channel(sr.alpha(dtype=torch.bfloat16), c)
+    return ops.patch_embed_read(x, emb.proj1.weight, emb.proj2.weight, emb.proj2.bias, alpha)
+
+
+def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    # the reference's lazy forward (local_thc.py:1374-1388) with the patch embedding
+    # and the shared read as one call
+    cond = self.t_embedder(t) + self.y_embedder(y)
+    t6 = self.shared_adaLN_modulation(cond)
+    t2 = self.shared_final_modulation(cond)
+    x0, z = _embed_and_read(self, x)
+    updates = []
+    for block in self.blocks:
+        dz = block.branch_update(z, t6, self.workspace_rope)
+        updates.append(dz)
+        z = block.lazy_workspace_update(z, dz, self.shared_read)
+    x_hi = self.final_accumulate_reference(x0, updates)
+    b, hh, wh, c_dim = x_hi.shape
+    return self.unpatchify(self.final_layer(x_hi.reshape(b, hh * wh, c_dim), t2))
+
+
 PATCHES = (
     ("SharedLocalRead", "read", _read),
     ("LayerLocalWrite", "write", _write),
@@ -106,6 +143,7 @@ PATCHES = (
     ("SharedReadFusedFinalLocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final_stacked),
     ("SharedReadFusedFinal12LocalTHCSharedAdaLNJiT", "final_accumulate_reference", _final12),
     ("FinalLayerSharedAdaLN", "forward", _final_layer),
+    ("SharedReadLocalTHCSharedAdaLNJiT", "forward_lazy", _forward_lazy),
 )
 
 

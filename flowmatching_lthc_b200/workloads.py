@@ -129,3 +129,16 @@ def final_bwd_bytes(B: int, T: int, C: int, act_bytes: int, w_bytes: int = 4) ->
     """Its backward: read x and grad m, write grad x; weight, scale rows and the
     fp32 weight / shift / scale gradients are small."""
     return 3 * B * T * C * act_bytes + C * w_bytes + B * C * act_bytes + (C + 2 * B * C) * 4
+
+
+def embed_bytes(B: int, H: int, C: int, in_ch: int = 3, img_bytes: int = 4) -> int:
+    """Patch embedding + read: read the images, write X0 [B,H,H,C] and Z [B,(H/4)^2,C]
+    in bf16, read the bf16 weights (479,203,072 B at B = 64, H = 64, C = 768)."""
+    return (B * in_ch * 16 * H * H * img_bytes + 2 * B * H * H * C + 2 * B * (H // 4) ** 2 * C
+            + 2 * (128 * in_ch * 16 + C * 128 + C + 16 * C))
+
+
+def embed_flops(B: int, H: int, C: int, in_ch: int = 3) -> int:
+    """Multiply-adds x 2 of the two convolutions as GEMMs (54.8 GFLOP at B = 64)."""
+    return 2 * B * H * H * (in_ch * 16 * 128 + 128 * C)
+
