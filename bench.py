@@ -188,18 +188,18 @@ def op_step(op: str, cfg: dict):
     x0, dz, P, g, alpha, z = cfg["x0"], cfg["dz"], cfg["P"], cfg["g"], cfg["alpha"], cfg["z"]
     beta = P[0].to(torch.bfloat16)
     table = {
-        "materialise_fwd": (lambda: ops.materialise(x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1,
+        "materialise_fwd": (lambda: ops.call(ops.materialise, x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1,
                             "broadcast_tma_kernel<bf16, 12, base>"),
-        "materialise_bwd": (lambda: ops.materialise_bwd(g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2), 2,
+        "materialise_bwd": (lambda: ops.call(ops.materialise_bwd, g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2), 2,
                             "pool_tma_kernel<bf16, 12, pool, wgrad> + reduce_partials_kernel"),
-        "read_fwd": (lambda: ops.read(x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
-        "read_bwd": (lambda: ops.read_bwd(x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
+        "read_fwd": (lambda: ops.call(ops.read, x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
+        "read_bwd": (lambda: ops.call(ops.read_bwd, x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
                      "broadcast_tma_kernel<bf16, 1> + pool_tma_kernel<bf16, 1, wgrad> + reduce_partials_kernel"),
-        "write_add_fwd": (lambda: ops.write_add(x0, dz[0], beta), W.write_add_bytes(B, G, C, 2, 2), 1,
+        "write_add_fwd": (lambda: ops.call(ops.write_add, x0, dz[0], beta), W.write_add_bytes(B, G, C, 2, 2), 1,
                           "broadcast_tma_kernel<bf16, 1, base>"),
-        "lazy_fwd": (lambda: ops.lazy_update(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 1,
+        "lazy_fwd": (lambda: ops.call(ops.lazy_update, z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 1,
                      "lazy_fwd_kernel<bf16>"),
-        "lazy_bwd": (lambda: ops.lazy_update_bwd(z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 2,
+        "lazy_bwd": (lambda: ops.call(ops.lazy_update_bwd, z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 2,
                      "lazy_bwd_kernel<bf16> + lazy_bwd_finalize_kernel"),
     }
     if op == "embed_fwd":
@@ -209,7 +209,7 @@ def op_step(op: str, cfg: dict):
         w1 = torch.randn(128, 3, 4, 4, device=x0.device, generator=gen) * 0.14
         w2 = torch.randn(C, 128, 1, 1, device=x0.device, generator=gen) * 0.09
         b2 = torch.randn(C, device=x0.device, generator=gen) * 0.1
-        table["embed_fwd"] = (lambda: ops.patch_embed_read(img, w1, w2, b2, alpha), W.embed_bytes(B, 4 * G, C), 1,
+        table["embed_fwd"] = (lambda: ops.call(ops.patch_embed_read, img, w1, w2, b2, alpha), W.embed_bytes(B, 4 * G, C), 1,
                               "patch_embed_read_kernel (tcgen05)")
     if op in ("final_fwd", "final_bwd"):
         # final-layer prologue on the materialised residual [B, 4096, 768] (FinalLayerSharedAdaLN)
@@ -218,9 +218,9 @@ def op_step(op: str, cfg: dict):
         nw = torch.ones(C, device=x0.device) + 0.1 * torch.randn(C, device=x0.device)
         t2 = (0.5 * torch.randn(B, 2 * C, device=x0.device)).to(torch.bfloat16)
         sh, sc = t2.chunk(2, dim=1)
-        table["final_fwd"] = (lambda: ops.final_norm_modulate(xt, nw, sh, sc, 1e-6), W.final_fwd_bytes(B, T, C, 2), 1,
+        table["final_fwd"] = (lambda: ops.call(ops.final_norm_modulate, xt, nw, sh, sc, 1e-6), W.final_fwd_bytes(B, T, C, 2), 1,
                               "final_norm_modulate_kernel<bf16, fwd>")
-        table["final_bwd"] = (lambda: ops.final_norm_modulate_bwd(gm, xt, nw, sc, 1e-6), W.final_bwd_bytes(B, T, C, 2),
+        table["final_bwd"] = (lambda: ops.call(ops.final_norm_modulate_bwd, gm, xt, nw, sc, 1e-6), W.final_bwd_bytes(B, T, C, 2),
                               2, "final_norm_modulate_kernel<bf16, bwd> + final_bwd_finalize_kernel")
     return table[op]
 

@@ -107,9 +107,17 @@ def check(status: int, func: str) -> None:
         raise LthcError(status, func, msg)
 
 
+_fns: dict = {}
+
+
 def call(func: str, *args) -> None:
     """Call an int-returning entry point and raise LthcError on failure."""
-    check(getattr(load(), func)(*args), func)
+    fn = _fns.get(func)
+    if fn is None or _lib is None:
+        fn = _fns[func] = getattr(load(), func)
+    st = fn(*args)
+    if st != 0:
+        check(st, func)
 
 
 def ptr_array(ptrs) -> ctypes.Array:

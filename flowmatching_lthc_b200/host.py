@@ -81,7 +81,7 @@ class HostMaterialiser:
                 ev_in.record(self.s_in)
             with torch.cuda.stream(self.s_comp):
                 self.s_comp.wait_event(ev_in)
-                out_d = ops.materialise(x0_d, dz_d, betas)
+                out_d = ops.call(ops.materialise, x0_d, dz_d, betas)
                 ev_c = torch.cuda.Event()
                 ev_c.record(self.s_comp)
             with torch.cuda.stream(self.s_out):

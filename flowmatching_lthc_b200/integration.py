@@ -40,7 +40,7 @@ def _read(self, x: torch.Tensor) -> torch.Tensor:
     hh = self.high_grid
     if h != hh or w != hh or c != self.hidden_size:
         raise ValueError(f"expected [B,{hh},{hh},{self.hidden_size}], got {tuple(x.shape)}")
-    return ops.read(x, per_channel(self.alpha(dtype=x.dtype), self.hidden_size))
+    return ops.call(ops.read, x, per_channel(self.alpha(dtype=x.dtype), self.hidden_size))
 
 
 def _check_dz(self, dz: torch.Tensor) -> None:
@@ -52,39 +52,39 @@ def _check_dz(self, dz: torch.Tensor) -> None:
 
 def _write(self, dz: torch.Tensor) -> torch.Tensor:
     _check_dz(self, dz)
-    return ops.write(dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+    return ops.call(ops.write, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
 
 
 def _write_add(self, x_hi: torch.Tensor, dz: torch.Tensor) -> torch.Tensor:
     _check_dz(self, dz)
-    return ops.write_add(x_hi, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+    return ops.call(ops.write_add, x_hi, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
 
 
 def _lazy_workspace_update(self, z: torch.Tensor, dz: torch.Tensor, shared_read) -> torch.Tensor:
     alpha = shared_read.alpha(dtype=dz.dtype)
     beta = self.write.beta(dtype=alpha.dtype)
     c = z.shape[-1]
-    return ops.lazy_update(z, dz, per_channel(alpha, c), per_channel(beta, c))
+    return ops.call(ops.lazy_update, z, dz, per_channel(alpha, c), per_channel(beta, c))
 
 
 def _final_loop(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
     # the pure-torch loop casts each beta to the update dtype (write_add)
     betas = [per_channel(b.write.beta(dtype=d.dtype), x0.shape[-1]) for b, d in zip(self.blocks, dz_list, strict=True)]
-    return ops.materialise(x0, list(dz_list), betas)
+    return ops.call(ops.materialise, x0, list(dz_list), betas)
 
 
 def _final_stacked(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
     betas = [per_channel(b.write.write_weight, x0.shape[-1]) for b in self.blocks]
     if len(dz_list) != len(betas):
         raise ValueError(f"got {len(dz_list)} workspace updates for {len(betas)} blocks")
-    return ops.materialise(x0, list(dz_list), betas)
+    return ops.call(ops.materialise, x0, list(dz_list), betas)
 
 
 def _final12(self, x0: torch.Tensor, dz_list: list[torch.Tensor]) -> torch.Tensor:
     if len(dz_list) != 12 or len(self.blocks) != 12:
         raise ValueError("SharedReadFusedFinal12LocalTHCSharedAdaLNJiT requires depth=12")
     betas = [per_channel(b.write.write_weight, x0.shape[-1]) for b in self.blocks]
-    return ops.materialise(x0, list(dz_list), betas)
+    return ops.call(ops.materialise, x0, list(dz_list), betas)
 
 
 def _final_layer(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
@@ -93,7 +93,7 @@ def _final_layer(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
     if x.dtype != shift.dtype or x.dim() != 3 or x.shape[-1] > ops.FINAL_MAX_CHANNELS:
         # a dtype mix the fused kernel does not take: the reference's own expression
         return self.linear(_ORIGINAL_MODULATE(norm(x), shift, scale))
-    return self.linear(ops.final_norm_modulate(x, norm.weight, shift, scale, norm.eps))
+    return self.linear(ops.call(ops.final_norm_modulate, x, norm.weight, shift, scale, norm.eps))
 
 
 _ORIGINAL_MODULATE = None
@@ -114,7 +114,7 @@ def _embed_and_read(model, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]
         return x0, sr.read(x0)
     c = emb.proj2.weight.shape[0]
     alpha = per_channel(sr.alpha(dtype=torch.bfloat16), c)
-    return ops.patch_embed_read(x, emb.proj1.weight, emb.proj2.weight, emb.proj2.bias, alpha)
+    return ops.call(ops.patch_embed_read, x, emb.proj1.weight, emb.proj2.weight, emb.proj2.bias, alpha)
 
 
 def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> torch.Tensor:

@@ -66,7 +66,7 @@ class SharedLocalRead(nn.Module):
         hh = self.high_grid
         if h != hh or w != hh or c != self.hidden_size:
             raise ValueError(f"expected [B,{hh},{hh},{self.hidden_size}], got {tuple(x.shape)}")
-        return ops.read(x, per_channel(self.alpha(dtype=x.dtype), self.hidden_size))
+        return ops.call(ops.read, x, per_channel(self.alpha(dtype=x.dtype), self.hidden_size))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self.read(x)
@@ -103,11 +103,11 @@ class LayerLocalWrite(nn.Module):
 
     def write(self, dz: torch.Tensor) -> torch.Tensor:
         self._check_dz(dz)
-        return ops.write(dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+        return ops.call(ops.write, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
 
     def write_add(self, x_hi: torch.Tensor, dz: torch.Tensor) -> torch.Tensor:
         self._check_dz(dz)
-        return ops.write_add(x_hi, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
+        return ops.call(ops.write_add, x_hi, dz, per_channel(self.beta(dtype=dz.dtype), self.hidden_size))
 
     def gamma_from_alpha(self, alpha: torch.Tensor) -> torch.Tensor:
         beta = self.beta(dtype=alpha.dtype)
@@ -124,7 +124,7 @@ def lazy_workspace_update(z: torch.Tensor, dz: torch.Tensor, shared_read: Shared
     alpha = shared_read.alpha(dtype=dz.dtype)
     beta = write.beta(dtype=alpha.dtype)
     c = z.shape[-1]
-    return ops.lazy_update(z, dz, per_channel(alpha, c), per_channel(beta, c))
+    return ops.call(ops.lazy_update, z, dz, per_channel(alpha, c), per_channel(beta, c))
 
 
 def final_accumulate(x0: torch.Tensor, dz_list: list[torch.Tensor], writes: list[LayerLocalWrite | nn.Module]) -> torch.Tensor:
@@ -133,7 +133,7 @@ def final_accumulate(x0: torch.Tensor, dz_list: list[torch.Tensor], writes: list
     if len(dz_list) != len(writes):
         raise ValueError(f"got {len(dz_list)} workspace updates for {len(writes)} write operators")
     c = x0.shape[-1]
-    return ops.materialise(x0, list(dz_list), [per_channel(w.write_weight, c) for w in writes])
+    return ops.call(ops.materialise, x0, list(dz_list), [per_channel(w.write_weight, c) for w in writes])
 
 
 __all__ = ["SharedLocalRead", "LayerLocalWrite", "lazy_workspace_update", "final_accumulate", "per_channel"]

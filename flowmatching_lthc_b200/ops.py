@@ -21,6 +21,9 @@ from typing import Sequence
 import torch
 from torch import Tensor
 
+from torch._subclasses.fake_tensor import FakeTensor
+from torch.utils._python_dispatch import _get_current_dispatch_mode as _current_dispatch_mode
+
 from . import _lib
 
 _DTYPE_CODE = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}
@@ -84,8 +87,53 @@ def _guard(t: Tensor):
     return torch.cuda.device(idx)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: Tensor) -> int:
+    """The current CUDA stream of t's device as a raw handle (without building a
+    torch.cuda.Stream object when torch offers the raw query)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t.device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+# The CUDA implementation of each operator, for calls that need neither autograd
+# nor a tracer (see call()).
+_DIRECT: dict = {}
+
+
+def _custom_op(name: str):
+    """torch.library.custom_op in the lthc_b200 namespace, CUDA only; the undecorated
+    implementation is kept for the direct call path."""
+    def deco(fn):
+        op = torch.library.custom_op(f"lthc_b200::{name}", mutates_args=(), device_types="cuda")(fn)
+        _DIRECT[id(op)] = fn
+        return op
+    return deco
+
+
+def _tensors(args):
+    for a in args:
+        if isinstance(a, Tensor):
+            yield a
+        elif isinstance(a, (list, tuple)):
+            yield from (t for t in a if isinstance(t, Tensor))
+
+
+def call(op, *args):
+    """Run `op` on args.  Calls that need no autograd graph (grad disabled or no
+    input requiring grad), are not being traced and hold real CUDA tensors go
+    straight to the CUDA implementation and skip the dispatcher's per-call cost
+    (tens of microseconds, comparable to the kernels of a small batch); every
+    other call goes through the registered operator."""
+    ts = list(_tensors(args))
+    fn = _DIRECT.get(id(op))
+    if (fn is None or torch.compiler.is_compiling() or _current_dispatch_mode() is not None
+            or any(t.device.type != "cuda" or isinstance(t, FakeTensor) for t in ts)
+            or (torch.is_grad_enabled() and any(t.requires_grad for t in ts))):
+        return op(*args)
+    return fn(*args)
 
 
 def _workspace(nbytes: int, device: torch.device) -> Tensor:
@@ -100,7 +148,7 @@ def _p(t: Tensor | None) -> int | None:
 # ---------------------------------------------------------------------------
 # read: residual [B,4G,4G,C] -> workspace [B,G*G,C]
 # ---------------------------------------------------------------------------
-@torch.library.custom_op("lthc_b200::read", mutates_args=(), device_types="cuda")
+@_custom_op("read")
 def read(x: Tensor, alpha: Tensor) -> Tensor:
     """z[b,cell,c] = sum_r alpha[c,r] x[b,cell,r,c]  (SharedLocalRead.read, local_thc.py:1211-1223)."""
     _require_cuda(x, alpha)
@@ -120,7 +168,7 @@ def _(x: Tensor, alpha: Tensor) -> Tensor:
     return x.new_empty((b, (h // 4) * (h // 4), c))
 
 
-@torch.library.custom_op("lthc_b200::read_bwd", mutates_args=(), device_types="cuda")
+@_custom_op("read_bwd")
 def read_bwd(x: Tensor, grad_z: Tensor, alpha: Tensor, need_grad_x: bool, need_grad_alpha: bool) -> tuple[Tensor, Tensor]:
     """grad_x = alpha (.) grad_z broadcast; grad_alpha = sum x*grad_z (fp32 [C,16])."""
     _require_cuda(x, grad_z, alpha)
@@ -194,7 +242,7 @@ def _materialise_impl(x0: Tensor | None, dz: Sequence[Tensor], beta: Sequence[Te
     return out
 
 
-@torch.library.custom_op("lthc_b200::materialise", mutates_args=(), device_types="cuda")
+@_custom_op("materialise")
 def materialise(x0: Tensor, dz: list[Tensor], beta: list[Tensor]) -> Tensor:
     """X_L = X_0 + sum_l beta_l (.) dz_l in one pass, fp32 accumulation, one rounding.
 
@@ -210,7 +258,7 @@ def _(x0, dz, beta):
     return torch.empty_like(x0)
 
 
-@torch.library.custom_op("lthc_b200::materialise_bwd", mutates_args=(), device_types="cuda")
+@_custom_op("materialise_bwd")
 def materialise_bwd(grad_out: Tensor, dz: list[Tensor], beta: list[Tensor], need_grad_dz: bool,
                     need_grad_beta: bool) -> tuple[list[Tensor], Tensor]:
     """grad_dz_l = sum_r beta_l grad_out (per cell); grad_beta = [L,C,16] fp32 sum grad_out*dz_l."""
@@ -269,7 +317,7 @@ def _materialise_backward(ctx, grad_out):
 materialise.register_autograd(_materialise_backward, setup_context=_materialise_setup)
 
 
-@torch.library.custom_op("lthc_b200::write", mutates_args=(), device_types="cuda")
+@_custom_op("write")
 def write(dz: Tensor, beta: Tensor) -> Tensor:
     """out[b,cell,r,c] = beta[c,r] dz[b,cell,c]  (LayerLocalWrite.write, local_thc.py:1261-1273)."""
     _require_cuda(dz, beta)
@@ -290,7 +338,7 @@ def _(dz, beta):
     return dz.new_empty((b, 4 * g, 4 * g, c))
 
 
-@torch.library.custom_op("lthc_b200::write_bwd", mutates_args=(), device_types="cuda")
+@_custom_op("write_bwd")
 def write_bwd(grad_out: Tensor, dz: Tensor, beta: Tensor, need_grad_dz: bool, need_grad_beta: bool) -> tuple[Tensor, Tensor]:
     """grad_dz = sum_r beta grad_out (per cell); grad_beta = sum grad_out*dz (fp32 [C,16])."""
     _require_cuda(grad_out, dz, beta)
@@ -333,7 +381,7 @@ def _write_backward(ctx, grad_out):
 write.register_autograd(_write_backward, setup_context=_write_setup)
 
 
-@torch.library.custom_op("lthc_b200::write_add", mutates_args=(), device_types="cuda")
+@_custom_op("write_add")
 def write_add(x_hi: Tensor, dz: Tensor, beta: Tensor) -> Tensor:
     """x_hi + write(dz)  (LayerLocalWrite.write_add, local_thc.py:1275-1276); fp32 sum, one rounding."""
     _require_cuda(x_hi, dz, beta)
@@ -375,7 +423,7 @@ write_add.register_autograd(_write_add_backward, setup_context=_write_add_setup)
 # ---------------------------------------------------------------------------
 # lazy shared-read recurrence  z' = z + gamma (.) dz,  gamma = sum_r alpha*beta
 # ---------------------------------------------------------------------------
-@torch.library.custom_op("lthc_b200::lazy_update", mutates_args=(), device_types="cuda")
+@_custom_op("lazy_update")
 def lazy_update(z: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor) -> Tensor:
     """Block.lazy_workspace_update with gamma_from_alpha (local_thc.py:1278-1283, 1325-1328)."""
     _require_cuda(z, dz, alpha, beta)
@@ -400,7 +448,7 @@ def _(z, dz, alpha, beta):
     return torch.empty_like(z)
 
 
-@torch.library.custom_op("lthc_b200::lazy_update_bwd", mutates_args=(), device_types="cuda")
+@_custom_op("lazy_update_bwd")
 def lazy_update_bwd(grad_z_out: Tensor, dz: Tensor, alpha: Tensor, beta: Tensor) -> tuple[Tensor, Tensor, Tensor]:
     """(grad_dz, grad_alpha fp32 [C,16], grad_beta fp32 [C,16]); grad_z is grad_z_out itself."""
     _require_cuda(grad_z_out, dz, alpha, beta)
@@ -446,7 +494,7 @@ lazy_update.register_autograd(_lazy_backward, setup_context=_lazy_setup)
 # ---------------------------------------------------------------------------
 # weight gradient  grad_w[l,c,r] = sum_cells high[cell,r,c] * low_l[cell,c]
 # ---------------------------------------------------------------------------
-@torch.library.custom_op("lthc_b200::weight_grad", mutates_args=(), device_types="cuda")
+@_custom_op("weight_grad")
 def weight_grad(high: Tensor, low: list[Tensor]) -> Tensor:
     """[L,C,16] fp32, reduced in a fixed order (replaces the atomics of
     _cell_weight_grad_kernel, local_thc_triton_kernels.py:167-199)."""
@@ -493,7 +541,7 @@ def embed_supported(img: Tensor, w1: Tensor, w2: Tensor) -> bool:
             and w2.shape[1] == 128 and tuple(w2.shape[2:]) == (1, 1) and w2.shape[0] % EMBED_CHUNK == 0)
 
 
-@torch.library.custom_op("lthc_b200::patch_embed_read", mutates_args=(), device_types="cuda")
+@_custom_op("patch_embed_read")
 def patch_embed_read(img: Tensor, w1: Tensor, w2: Tensor, b2: Tensor, alpha: Tensor) -> tuple[Tensor, Tensor]:
     """(X0 [B,H,H,C] bf16, Z [B,(H/4)^2,C] bf16): both convolutions in bf16 with fp32
     accumulation on the tensor cores, then the read of X0 with alpha."""
@@ -605,7 +653,7 @@ def _mod_rows(shift: Tensor, scale: Tensor) -> tuple[Tensor, Tensor, int]:
     return shift.contiguous(), scale.contiguous(), c
 
 
-@torch.library.custom_op("lthc_b200::final_norm_modulate", mutates_args=(), device_types="cuda")
+@_custom_op("final_norm_modulate")
 def final_norm_modulate(x: Tensor, weight: Tensor, shift: Tensor, scale: Tensor, eps: float) -> Tensor:
     """modulate(RMSNorm(x) with weight and eps, shift, scale) over tokens [B,T,C]."""
     _require_cuda(x, weight, shift, scale)
@@ -625,7 +673,7 @@ def _(x, weight, shift, scale, eps):
     return torch.empty_like(x)
 
 
-@torch.library.custom_op("lthc_b200::final_norm_modulate_bwd", mutates_args=(), device_types="cuda")
+@_custom_op("final_norm_modulate_bwd")
 def final_norm_modulate_bwd(grad_out: Tensor, x: Tensor, weight: Tensor, scale: Tensor,
                             eps: float) -> tuple[Tensor, Tensor, Tensor, Tensor]:
     """(grad_x, grad_weight fp32 [C], grad_shift fp32 [B,C], grad_scale fp32 [B,C])."""

@@ -78,3 +78,17 @@ def test_reference_op_mirrors_exist():
         assert callable(getattr(ops, name))
     with pytest.raises(ValueError):
         ops.final_accumulate_b4_12_traceable(torch.zeros(1), torch.zeros(1))
+
+
+def test_call_routes_meta_and_cpu_tensors_through_the_dispatcher():
+    """ops.call takes the direct CUDA path only for real CUDA tensors without an
+    autograd graph; meta tensors get the registered fake implementation and CPU
+    tensors the operator's own error."""
+    m = torch.empty(2, 64, 768, device="meta", dtype=torch.bfloat16)
+    w = torch.empty(768, 16, device="meta", dtype=torch.bfloat16)
+    out = ops.call(ops.lazy_update, m, m, w, w)
+    assert out.device.type == "meta" and out.shape == m.shape
+    c = torch.zeros(2, 64, 768, dtype=torch.bfloat16)
+    wc = torch.zeros(768, 16, dtype=torch.bfloat16)
+    with pytest.raises((ValueError, NotImplementedError)):
+        ops.call(ops.lazy_update, c, c, wc, wc)

@@ -421,3 +421,19 @@ def test_torch_compile_fullgraph_forward_and_backward():
     compiled = run(torch.compile(f, fullgraph=True))
     for e, c in zip(eager, compiled):
         assert same_bits(c, e) or rel_err(c, e) < RTOL_REDUCTION
+
+
+def test_direct_call_path_matches_the_operator():
+    """ops.call: the direct CUDA path (no autograd needed) gives the operator's
+    bits; with an input that requires grad it goes through the operator and
+    records the autograd graph."""
+    x = rnd(2, 16, 16, 64, dtype=torch.bfloat16, seed=600).cuda()
+    alpha = rnd(64, 16, dtype=torch.bfloat16, seed=601).cuda()
+    ref = ops.read(x, alpha)
+    assert same_bits(ops.call(ops.read, x, alpha), ref)
+    xr = x.clone().requires_grad_(True)
+    out = ops.call(ops.read, xr, alpha)
+    assert out.grad_fn is not None and same_bits(out, ref)
+    with torch.no_grad():
+        out2 = ops.call(ops.read, xr, alpha)
+    assert out2.grad_fn is None and same_bits(out2, ref)
