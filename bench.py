@@ -17,6 +17,8 @@ flush is needed between steps.
 from __future__ import annotations
 
 import argparse
+import contextlib
+import ctypes
 import json
 import os
 import shutil
@@ -420,9 +422,29 @@ def config_dict(B: int, world: int, op: str = "materialise_fwd") -> dict:
 
 
 # ------------------------------------------------------------------ our arm
+@contextlib.contextmanager
+def _stdout_to_stderr():
+    """Send everything written to file descriptor 1 (Python and C stdio alike) to
+    stderr, so that stdout carries only the one JSON result line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        try:
+            ctypes.CDLL(None).fflush(None)
+        except OSError:
+            pass
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def main() -> int:
     args = parse_args()
     r = D.from_env()
+
     if args.impl == "reference":
         return reference_arm(args, r)
 
@@ -433,7 +455,9 @@ def main() -> int:
         return 1
     torch.cuda.set_device(r.local_rank)
     dev = torch.device("cuda", r.local_rank)
-    D.init("nccl", r, device=dev)
+    with _stdout_to_stderr():  # the communicator set-up prints a version banner on stdout
+        D.init("nccl", r, device=dev)
+        D.barrier()
     stream = torch.cuda.current_stream(dev)
     B = args.batch
 
