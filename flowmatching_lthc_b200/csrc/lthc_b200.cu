@@ -460,6 +460,10 @@ struct FinalShape {
 #define LTHC_FINAL_BWD_STAGES 3
 #endif
 constexpr size_t kFinalSmemBudget = LTHC_FINAL_SMEM_BUDGET_KB * 1024;
+// The ring refills the stage of tile i - 1 at the end of tile i (after that
+// tile's bulk store has read it) with tile i - 1 + stages, while tile i + 1 must
+// already be loading: fewer than 3 stages would wait on a tile never requested.
+static_assert(LTHC_FINAL_FWD_STAGES >= 3 && LTHC_FINAL_BWD_STAGES >= 3, "the final-layer ring needs 3 or more stages");
 
 FinalShape final_shape(int64_t C, int es, bool bwd) {
   FinalShape f;
