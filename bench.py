@@ -213,6 +213,18 @@ def op_step(op: str, cfg: dict):
         b2 = torch.randn(C, device=x0.device, generator=gen) * 0.1
         table["embed_fwd"] = (lambda: ops.call(ops.patch_embed_read, img, w1, w2, b2, alpha), W.embed_bytes(B, 4 * G, C), 1,
                               "patch_embed_read_kernel (tcgen05)")
+    if op in ("branch_fwd", "branch_bwd"):
+        # branch epilogue + lazy update on the workspace rows [B, 256, 768]; gate is a chunk of t6
+        gen = torch.Generator(device=x0.device).manual_seed(13)
+        attn = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
+        mlp = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
+        gate = (0.5 * torch.randn(B, 6 * C, device=x0.device, generator=gen)).to(torch.bfloat16).chunk(6, dim=-1)[5]
+        n = B * G * G
+        table["branch_fwd"] = (lambda: ops.call(ops.branch_lazy_update, z, attn, mlp, gate, alpha, beta),
+                               W.branch_fwd_bytes(n, B, C, 2, 2), 1, "branch_lazy_fwd_kernel<bf16>")
+        table["branch_bwd"] = (lambda: ops.call(ops.branch_lazy_update_bwd, attn, z, mlp, attn, gate, alpha, beta),
+                               W.branch_bwd_bytes(n, B, C, 2, 2), 2,
+                               "branch_lazy_bwd_kernel<bf16> + branch_lazy_bwd_finalize_kernel")
     if op in ("final_fwd", "final_bwd"):
         # final-layer prologue on the materialised residual [B, 4096, 768] (FinalLayerSharedAdaLN)
         T = 16 * G * G
@@ -228,7 +240,7 @@ def op_step(op: str, cfg: dict):
 
 
 OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
-       "final_fwd", "final_bwd", "embed_fwd")
+       "final_fwd", "final_bwd", "embed_fwd", "branch_fwd", "branch_bwd")
 MODEL_OPS = ("model_fwd", "train_step", "sample")
 # Largest batch per model call for which the reference Triton materialisation's
 # 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
@@ -409,6 +421,8 @@ WORKLOADS = {
     "lazy_bwd": "lazy update bwd, config 2 shapes",
     "final_fwd": "final-layer RMSNorm + AdaLN modulate on X_L [B, 4096, 768], config 2 shapes",
     "final_bwd": "final-layer RMSNorm + modulate bwd (grad X_L, grad norm weight / shift / scale), config 2 shapes",
+    "branch_fwd": "branch output sum (dz_attn + gate*mlp_out) fused with the lazy update, config 2 workspace shapes",
+    "branch_bwd": "its backward (grad dz_attn / mlp_out / gate / alpha / beta), config 2 workspace shapes",
     "embed_fwd": "patch embedding (4x4 conv 3->128, 1x1 conv 128->768) + shared read, config 3 images, tcgen05",
 }
 
@@ -617,6 +631,24 @@ def measure_kernels(cfg: dict, stream, peak) -> dict:
                               "host_us_per_call": round(host_us, 1)}
 
     B, x0, dz, P, g = cfg["B"], cfg["x0"], cfg["dz"], cfg["P"], cfg["g"]
+    # the reference's eager epilogue + lazy update (local_thc.py:321-323, 1326-1328):
+    # four elementwise torch kernels plus the gamma reduction, on the same inputs
+    gen = torch.Generator(device=x0.device).manual_seed(13)
+    attn = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
+    mlp = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
+    gate = (0.5 * torch.randn(B, 6 * C, device=x0.device, generator=gen)).to(torch.bfloat16).chunk(6, dim=-1)[5]
+    alpha, beta, z = cfg["alpha"], P[0].to(torch.bfloat16), cfg["z"]
+
+    def eager_branch():
+        d = attn + gate.unsqueeze(1) * mlp
+        return d, z + (alpha * beta).sum(-1)[None, None, :] * d
+
+    eager_branch()
+    ms = time_device(eager_branch, iters, stream)
+    nb = W.branch_fwd_bytes(B * G * G, B, C, 2, 2)
+    out["comparators"]["eager_branch_epilogue_lazy"] = {
+        "ms": round(ms, 4), "gbs": round(nb / (ms / 1e3) / 1e9, 1),
+        "speedup_of_ours": round(ms / out["kernels"]["branch_fwd"]["ms"], 3)}
     ref = ROOT / "baseline" / "_ref"
     if (ref / "flowmatching_lthc").exists():
         try:

@@ -58,6 +58,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_lazy_update_bwd_workspace_bytes": (c_size_t, [_L, _L]),
     "lthc_lazy_update_bwd": (_I, [_P, _P, _P, _I, _P, _I, _P, _P, _P, _P, c_size_t, _L, _L, _I, _P]),
     "lthc_selftest_umma": (_I, [_P, _P, _P, _I, _I, _P, _P]),
+    "lthc_branch_lazy_fwd": (_I, [_P, _P, _P, _P, _L, _P, _I, _P, _I, _P, _P, _L, _L, _L, _I, _P]),
+    "lthc_branch_lazy_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
+    "lthc_branch_lazy_bwd": (_I, [_P, _P, _P, _P, _P, _L, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, c_size_t, _L, _L,
+                                  _L, _I, _P]),
     "lthc_patch_embed_read_fwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _L, _I, _L, _L, _P]),
     "lthc_final_norm_modulate_fwd": (_I, [_P, _P, _I, _P, _P, _L, _P, _L, _L, _L, c_float, _I, _P]),
     "lthc_final_norm_modulate_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),

@@ -21,6 +21,7 @@
 #include "lthc_final.cuh"
 #include "lthc_umma.cuh"
 #include "lthc_embed.cuh"
+#include "lthc_branch.cuh"
 
 namespace lthc {
 
@@ -413,6 +414,33 @@ int read_family(const ReadJob& j, size_t ws_bytes, int act, cudaStream_t s) {
 int check_weight_dtype(int dt, const char* name) {
   if (!valid_act(dt)) return fail(LTHC_ERR_DTYPE, "unknown %s dtype code %d", name, dt);
   return LTHC_OK;
+}
+
+// ---- branch epilogue fused with the lazy update -------------------------------
+
+// Backward CTAs per image (each owns a contiguous row range of one image); a
+// pure function of the shape and the SM count, so that the workspace query and
+// the launch agree.
+int64_t branch_ctas_per_image(int64_t B, int64_t T, int64_t C, int sms) {
+  if (B <= 0 || T <= 0) return 1;
+  const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(sms) * 4 / lazy_slices(C, 4));
+  const int64_t k = std::max<int64_t>(1, std::min<int64_t>(ceil_div(target, B), ceil_div(T, kLazyWarps)));
+  return ceil_div(T, ceil_div(T, k));
+}
+
+size_t branch_ws_bytes(int64_t B, int64_t T, int64_t C, int sms) {
+  if (B <= 0 || T <= 0) return 0;
+  return static_cast<size_t>(B * branch_ctas_per_image(B, T, C, sms)) * 2 * C * sizeof(float);
+}
+
+int check_branch(int64_t B, int64_t T, int64_t C, int64_t gstride, int act, int adt, int bdt) {
+  if (B < 0 || T < 0) return fail(LTHC_ERR_SHAPE, "batch and rows per image must be >= 0");
+  if (C < 8 || C > 16384 || C % 8) return fail(LTHC_ERR_SHAPE, "channels must be a multiple of 8 in [8, 16384]");
+  if (gstride < C || gstride % 8) return fail(LTHC_ERR_SHAPE, "gate row stride %lld must be >= C and a multiple of 8",
+                                              (long long)gstride);
+  if (!valid_act(act)) return fail(LTHC_ERR_DTYPE, "unknown activation dtype code %d", act);
+  LTHC_TRY(check_weight_dtype(adt, "alpha"));
+  return check_weight_dtype(bdt, "beta");
 }
 
 // ---- patch embedding fused with the shared read (tensor cores) -----------------
@@ -924,12 +952,131 @@ int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const void* alp
   }
   LTHC_TRY(launched("lazy update backward"));
   if (grad_alpha || grad_beta) {
-    const int64_t n = C * kPos;
-    lazy_bwd_finalize_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(p, static_cast<int>(nblk),
-                                                                                      grad_alpha, grad_beta);
+    lazy_bwd_finalize_kernel<<<static_cast<unsigned>(ceil_div(C, 32)), 32 * kGammaFinalizeWarps, 0, s>>>(
+        p, static_cast<int>(nblk), grad_alpha, grad_beta);
     LTHC_TRY(launched("lazy update backward finalize"));
   }
   return LTHC_OK;
+}
+
+// ------------------- branch epilogue fused with the lazy update ----------------
+
+int lthc_branch_lazy_fwd(const void* z, const void* dz_attn, const void* mlp_out, const void* gate,
+                         int64_t gate_stride, const void* alpha, int alpha_dtype, const void* beta, int beta_dtype,
+                         void* dz_out, void* z_out, int64_t B, int64_t T, int64_t C, int act_dtype, void* stream) {
+  LTHC_TRY(check_branch(B, T, C, gate_stride, act_dtype, alpha_dtype, beta_dtype));
+  const bool ne = B > 0 && T > 0;
+  LTHC_TRY(check_act(z, "z", ne));
+  LTHC_TRY(check_act(dz_attn, "dz_attn", ne));
+  LTHC_TRY(check_act(mlp_out, "mlp_out", ne));
+  LTHC_TRY(check_act(gate, "gate", ne));
+  LTHC_TRY(check_act(dz_out, "dz_out", ne));
+  LTHC_TRY(check_act(z_out, "z_out", ne));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  if (!ne) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  BranchLazyParams p;
+  memset(&p, 0, sizeof(p));
+  p.z = z;
+  p.attn = dz_attn;
+  p.mlp = mlp_out;
+  p.gate = gate;
+  p.a = alpha;
+  p.b = beta;
+  p.a_dtype = alpha_dtype;
+  p.b_dtype = beta_dtype;
+  p.out0 = dz_out;
+  p.out1 = z_out;
+  p.N = B * T;
+  p.C = C;
+  p.T = T;
+  p.gstride = gate_stride;
+  const int es = act_dtype == LTHC_DTYPE_F32 ? 4 : 2;
+  const dim3 grid(static_cast<unsigned>(lazy_row_blocks(p.N, C, sms)), static_cast<unsigned>(lazy_slices(C, es)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (act_dtype) {
+    case LTHC_DTYPE_F32: branch_lazy_fwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    case LTHC_DTYPE_BF16: branch_lazy_fwd_kernel<__nv_bfloat16><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    default: branch_lazy_fwd_kernel<__half><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+  }
+  return launched("branch epilogue + lazy update");
+}
+
+size_t lthc_branch_lazy_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C) {
+  if (C <= 0) return 0;
+  return branch_ws_bytes(B, T, C, sms_for_sizing());
+}
+
+int lthc_branch_lazy_bwd(const void* grad_dz, const void* grad_z_out, const void* dz, const void* mlp_out,
+                         const void* gate, int64_t gate_stride, const void* alpha, int alpha_dtype, const void* beta,
+                         int beta_dtype, void* grad_attn, void* grad_mlp, float* grad_gate, float* grad_alpha,
+                         float* grad_beta, void* workspace, size_t workspace_bytes, int64_t B, int64_t T, int64_t C,
+                         int act_dtype, void* stream) {
+  LTHC_TRY(check_branch(B, T, C, gate_stride, act_dtype, alpha_dtype, beta_dtype));
+  const bool ne = B > 0 && T > 0;
+  if (grad_dz) LTHC_TRY(check_act(grad_dz, "grad_dz", ne));
+  LTHC_TRY(check_act(grad_z_out, "grad_z_out", ne));
+  LTHC_TRY(check_act(dz, "dz", ne));
+  LTHC_TRY(check_act(mlp_out, "mlp_out", ne));
+  LTHC_TRY(check_act(gate, "gate", ne));
+  LTHC_TRY(check_act(grad_attn, "grad_attn", ne));
+  LTHC_TRY(check_act(grad_mlp, "grad_mlp", ne));
+  LTHC_TRY(check_ptr(alpha, "alpha"));
+  LTHC_TRY(check_ptr(beta, "beta"));
+  if (!ne && !grad_alpha && !grad_beta && (B == 0 || !grad_gate)) return LTHC_OK;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!ne) {
+    if (grad_alpha && cudaMemsetAsync(grad_alpha, 0, sizeof(float) * C * kPos, s) != cudaSuccess)
+      return launched("memset");
+    if (grad_beta && cudaMemsetAsync(grad_beta, 0, sizeof(float) * C * kPos, s) != cudaSuccess)
+      return launched("memset");
+    if (B > 0 && grad_gate && cudaMemsetAsync(grad_gate, 0, sizeof(float) * B * C, s) != cudaSuccess)
+      return launched("memset");
+    return LTHC_OK;
+  }
+  const size_t need = branch_ws_bytes(B, T, C, sms);
+  if (!workspace || workspace_bytes < need)
+    return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
+                need);
+  if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+  const int64_t per_image = branch_ctas_per_image(B, T, C, sms);
+  BranchLazyParams p;
+  memset(&p, 0, sizeof(p));
+  p.mlp = mlp_out;
+  p.gate = gate;
+  p.a = alpha;
+  p.b = beta;
+  p.a_dtype = alpha_dtype;
+  p.b_dtype = beta_dtype;
+  p.dz = dz;
+  p.g_dz = grad_dz;
+  p.g_zo = grad_z_out;
+  p.out0 = grad_attn;
+  p.out1 = grad_mlp;
+  p.partial = static_cast<float*>(workspace);
+  p.N = B * T;
+  p.C = C;
+  p.T = T;
+  p.gstride = gate_stride;
+  p.rows_per_cta = ceil_div(T, per_image);
+  const int es = act_dtype == LTHC_DTYPE_F32 ? 4 : 2;
+  const dim3 grid(static_cast<unsigned>(B * per_image), static_cast<unsigned>(lazy_slices(C, es)));
+  switch (act_dtype) {
+    case LTHC_DTYPE_F32: branch_lazy_bwd_kernel<float><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    case LTHC_DTYPE_BF16: branch_lazy_bwd_kernel<__nv_bfloat16><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+    default: branch_lazy_bwd_kernel<__half><<<grid, 32 * kLazyWarps, 0, s>>>(p); break;
+  }
+  LTHC_TRY(launched("branch epilogue + lazy update backward"));
+  const int64_t gate_blocks = grad_gate ? std::min<int64_t>(ceil_div(B * C, 32 * kGammaFinalizeWarps),
+                                                             static_cast<int64_t>(sms) * 4) : 0;
+  const int64_t blocks = ceil_div(C, 32) + gate_blocks;
+  branch_lazy_bwd_finalize_kernel<<<static_cast<unsigned>(blocks), 32 * kGammaFinalizeWarps, 0, s>>>(
+      p, B, per_image, grad_gate, grad_alpha, grad_beta);
+  return launched("branch epilogue + lazy update backward finalize");
 }
 
 // ------------------- patch embedding fused with the shared read ----------------
@@ -1040,10 +1187,13 @@ int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight, int w_d
   int64_t K = 0;
   LTHC_TRY(final_dispatch<true>(p, B, sms, &K, act_dtype, s));
   if (grad_weight || grad_shift || grad_scale) {
-    const int64_t total = C + 2 * B * C;
-    const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(sms) * 8);
-    final_bwd_finalize_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p.partial, grad_weight, grad_shift,
-                                                                             grad_scale, B, K, C);
+    const int64_t img_blocks = (grad_shift || grad_scale)
+                                   ? std::min<int64_t>(ceil_div(2 * B * C, 32 * kGammaFinalizeWarps),
+                                                       static_cast<int64_t>(sms) * 4)
+                                   : 0;
+    const int64_t blocks = ceil_div(C, 32) + img_blocks;
+    final_bwd_finalize_kernel<<<static_cast<unsigned>(blocks), 32 * kGammaFinalizeWarps, 0, s>>>(
+        p.partial, grad_weight, grad_shift, grad_scale, B, K, C);
     LTHC_TRY(launched("final norm/modulate backward finalize"));
   }
   return LTHC_OK;

@@ -31,6 +31,7 @@
 #pragma once
 
 #include "lthc_common.cuh"
+#include "lthc_kernels.cuh"
 #include "lthc_tma.cuh"
 
 namespace lthc {
@@ -347,29 +348,34 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
   }
 }
 
-// Sums the per-CTA partials in CTA order: grad w over every CTA, grad shift and
-// grad scale over the CTAs of each image.  One thread per output element.
-__global__ void final_bwd_finalize_kernel(const float* __restrict__ partial, float* grad_w, float* grad_shift,
-                                          float* grad_scale, int64_t B, int64_t per_image, int64_t C) {
-  const int64_t n_w = grad_w ? C : 0;
-  const int64_t n_img = B * C;
-  const int64_t total = n_w + 2 * n_img;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    if (idx < n_w) {
-      float s = 0.f;
-      for (int64_t k = 0; k < B * per_image; ++k) s = __fadd_rn(s, partial[(k * 3 + 0) * C + idx]);
-      grad_w[idx] = s;
-    } else {
-      const int64_t e = idx - n_w;
-      const int q = e < n_img ? 1 : 2;
-      const int64_t be = e < n_img ? e : e - n_img;
-      const int64_t b = be / C, c = be - b * C;
-      float s = 0.f;
-      for (int64_t k = 0; k < per_image; ++k) s = __fadd_rn(s, partial[((b * per_image + k) * 3 + q) * C + c]);
-      float* dst = q == 1 ? grad_shift : grad_scale;
-      if (dst) dst[be] = s;
+// Sums the per-CTA partials in a fixed order: blocks [0, ceil(C/32)) form grad w
+// over every CTA (column_sum32), the remaining blocks grad shift and grad scale
+// over the CTAs of each image (CTA order), one thread per output element.
+__global__ void __launch_bounds__(32 * kGammaFinalizeWarps) final_bwd_finalize_kernel(
+    const float* __restrict__ partial, float* grad_w, float* grad_shift, float* grad_scale, int64_t B,
+    int64_t per_image, int64_t C) {
+  const int64_t w_blocks = (C + 31) / 32;
+  if (blockIdx.x < w_blocks) {
+    if (grad_w) {
+      __shared__ float tot[32];
+      const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 32;
+      column_sum32(partial, B * per_image, 3 * C, C, c0, tot);
+      if (threadIdx.x < 32 && c0 + threadIdx.x < C) grad_w[c0 + threadIdx.x] = tot[threadIdx.x];
     }
+    return;
+  }
+  if (!grad_shift && !grad_scale) return;
+  const int64_t n_img = B * C;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x - w_blocks) * blockDim.x;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x - w_blocks) * blockDim.x + threadIdx.x; e < 2 * n_img;
+       e += nthreads) {
+    const int q = e < n_img ? 1 : 2;
+    const int64_t be = e < n_img ? e : e - n_img;
+    const int64_t b = be / C, c = be - b * C;
+    float s = 0.f;
+    for (int64_t k = 0; k < per_image; ++k) s = __fadd_rn(s, partial[((b * per_image + k) * 3 + q) * C + c]);
+    float* dst = q == 1 ? grad_shift : grad_scale;
+    if (dst) dst[be] = s;
   }
 }
 

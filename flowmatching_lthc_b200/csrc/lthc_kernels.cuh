@@ -212,17 +212,67 @@ __global__ void __launch_bounds__(256) lazy_bwd_kernel(const __grid_constant__ L
   }
 }
 
-// ggamma[c] = sum_k partial[k][c];  grad_a[c,r] = ggamma*b[c,r];  grad_b[c,r] = ggamma*a[c,r]
-__global__ void __launch_bounds__(256) lazy_bwd_finalize_kernel(const __grid_constant__ LazyParams p, int nblk,
-                                                                float* __restrict__ grad_a,
-                                                                float* __restrict__ grad_b) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (c, r)
-  if (i >= p.C * kPos) return;
-  const int64_t c = i / kPos;
+// ggamma[c] = sum_k partial[k * kstride + c];  grad_a[c,r] = ggamma*b[c,r];
+// grad_b[c,r] = ggamma*a[c,r].  One block per 32 channels: warp w sums the
+// partials k = w, w + 8, ... (coalesced over the channels, eight independent
+// chains instead of one chain of nblk dependent adds), the eight warp sums are
+// added in warp order, then the block writes its 32 x 16 outputs.  Fixed order:
+// bitwise reproducible.
+constexpr int kGammaFinalizeWarps = 8;
+
+// Fixed-order column sums of 32 channels c0 .. c0+31 over nblk partial rows
+// (row k at partial + k * kstride) by a block of kGammaFinalizeWarps warps; the
+// result lands in tot[0..31] (shared), visible to the whole block on return.
+__device__ __forceinline__ void column_sum32(const float* __restrict__ partial, int64_t nblk, int64_t kstride,
+                                             int64_t C, int64_t c0, float* tot) {
+  __shared__ float red[kGammaFinalizeWarps][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t c = c0 + lane;
   float s = 0.f;
-  for (int k = 0; k < nblk; ++k) s += p.partial[static_cast<int64_t>(k) * p.C + c];
-  if (grad_a) grad_a[i] = s * load_weight(p.b, p.b_dtype, i);
-  if (grad_b) grad_b[i] = s * load_weight(p.a, p.a_dtype, i);
+  if (c < C) {
+    int64_t k = warp;
+    for (; k + 3 * kGammaFinalizeWarps < nblk; k += 4 * kGammaFinalizeWarps) {
+      const float v0 = partial[k * kstride + c];
+      const float v1 = partial[(k + kGammaFinalizeWarps) * kstride + c];
+      const float v2 = partial[(k + 2 * kGammaFinalizeWarps) * kstride + c];
+      const float v3 = partial[(k + 3 * kGammaFinalizeWarps) * kstride + c];
+      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
+    }
+    for (; k < nblk; k += kGammaFinalizeWarps) s = __fadd_rn(s, partial[k * kstride + c]);
+  }
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGammaFinalizeWarps; ++w) t = __fadd_rn(t, red[w][lane]);
+    tot[lane] = t;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void gamma_grad_block(const float* __restrict__ partial, int64_t nblk, int64_t kstride,
+                                                 int64_t C, int64_t c0, const void* a, int a_dtype, const void* b,
+                                                 int b_dtype, float* grad_a, float* grad_b) {
+  __shared__ float tot[32];
+  column_sum32(partial, nblk, kstride, C, c0, tot);
+  for (int i = threadIdx.x; i < 32 * kPos; i += blockDim.x) {
+    const int64_t cc = c0 + i / kPos;
+    if (cc < C) {
+      const int64_t idx = cc * kPos + i % kPos;
+      const float g = tot[i / kPos];
+      if (grad_a) grad_a[idx] = g * load_weight(b, b_dtype, idx);
+      if (grad_b) grad_b[idx] = g * load_weight(a, a_dtype, idx);
+    }
+  }
+}
+
+// grid: ceil(C / 32) blocks of 32 * kGammaFinalizeWarps threads
+__global__ void __launch_bounds__(32 * kGammaFinalizeWarps) lazy_bwd_finalize_kernel(
+    const __grid_constant__ LazyParams p, int nblk, float* __restrict__ grad_a, float* __restrict__ grad_b) {
+  gamma_grad_block(p.partial, nblk, p.C, p.C, static_cast<int64_t>(blockIdx.x) * 32, p.a, p.a_dtype, p.b, p.b_dtype,
+                   grad_a, grad_b);
 }
 
 }  // namespace lthc

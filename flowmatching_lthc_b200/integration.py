@@ -17,7 +17,8 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   SharedReadFusedFinal12LocalTHCSharedAdaLNJiT.final_accumulate_reference :1416-1420 (released op)
   FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
   SharedReadLocalTHCSharedAdaLNJiT.forward_lazy (patch embedding + shared read
-      fused on the tensor cores under bf16 autocast)                           :1374-1388
+      fused on the tensor cores under bf16 autocast; each block's branch
+      epilogue, :318-323, fused with its lazy update)                           :1374-1388
 
 Shape checks and messages are the reference's own; the arithmetic runs in
 ``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
@@ -97,6 +98,7 @@ def _final_layer(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
 
 
 _ORIGINAL_MODULATE = None
+_LTHC = None  # the patched reference module
 
 
 def _embed_and_read(model, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -117,6 +119,30 @@ def _embed_and_read(model, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]
     return ops.call(ops.patch_embed_read, x, emb.proj1.weight, emb.proj2.weight, emb.proj2.bias, alpha)
 
 
+def _branch_and_update(block, z: torch.Tensor, t6: torch.Tensor, rope, shared_read) -> tuple[torch.Tensor, torch.Tensor]:
+    """dz = block.branch_update(z, t6, rope) and z' = block.lazy_workspace_update(z, dz,
+    shared_read), with the branch's output epilogue (gate product and sum,
+    local_thc.py:318-323) and the lazy update as one pass over the rows.  Other
+    branch types, overridden methods and dtype mixes take the two calls."""
+    br = block.branch
+    fused = (_LTHC is not None and type(br).forward is _LTHC.WorkspaceSharedAdaLNBranch.forward
+             and type(block).branch_update is _LTHC.SharedReadLocalTHCSharedAdaLNJiTBlock.branch_update
+             and type(block).lazy_workspace_update is _lazy_workspace_update and z.is_cuda and z.dim() == 3)
+    if not fused:
+        dz = block.branch_update(z, t6, rope)
+        return dz, block.lazy_workspace_update(z, dz, shared_read)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = t6.chunk(6, dim=-1)
+    dz_attn = gate_msa.unsqueeze(1) * br.attn(_ORIGINAL_MODULATE(br.norm1(z), shift_msa, scale_msa), rope)
+    mlp_out = br.mlp(_ORIGINAL_MODULATE(br.norm2(z + dz_attn), shift_mlp, scale_mlp))
+    if not (z.dtype == dz_attn.dtype == mlp_out.dtype == gate_mlp.dtype):
+        dz = dz_attn + gate_mlp.unsqueeze(1) * mlp_out
+        return dz, block.lazy_workspace_update(z, dz, shared_read)
+    alpha = shared_read.alpha(dtype=dz_attn.dtype)
+    beta = block.write.beta(dtype=alpha.dtype)
+    c = z.shape[-1]
+    return ops.call(ops.branch_lazy_update, z, dz_attn, mlp_out, gate_mlp, per_channel(alpha, c), per_channel(beta, c))
+
+
 def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     # the reference's lazy forward (local_thc.py:1374-1388) with the patch embedding
     # and the shared read as one call
@@ -126,9 +152,8 @@ def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> to
     x0, z = _embed_and_read(self, x)
     updates = []
     for block in self.blocks:
-        dz = block.branch_update(z, t6, self.workspace_rope)
+        dz, z = _branch_and_update(block, z, t6, self.workspace_rope, self.shared_read)
         updates.append(dz)
-        z = block.lazy_workspace_update(z, dz, self.shared_read)
     x_hi = self.final_accumulate_reference(x0, updates)
     b, hh, wh, c_dim = x_hi.shape
     return self.unpatchify(self.final_layer(x_hi.reshape(b, hh * wh, c_dim), t2))
@@ -171,8 +196,9 @@ def install(local_thc: ModuleType | None = None) -> Installation:
     """Route the reference model's LTHC methods through the B200 kernels."""
     if local_thc is None:
         local_thc = importlib.import_module("flowmatching_lthc.models.local_thc")
-    global _ORIGINAL_MODULATE
+    global _ORIGINAL_MODULATE, _LTHC
     _ORIGINAL_MODULATE = local_thc.modulate
+    _LTHC = local_thc
     inst = Installation(local_thc)
     for cls_name, meth, fn in PATCHES:
         cls = getattr(local_thc, cls_name, None)

@@ -523,6 +523,114 @@ def _(high, low):
 
 
 # ---------------------------------------------------------------------------
+# branch epilogue fused with the lazy update
+# (WorkspaceSharedAdaLNBranch.forward's output sum, local_thc.py:318-323, then
+# lazy_workspace_update, :1325-1328)
+# ---------------------------------------------------------------------------
+def _branch_geom(z: Tensor, dz_attn: Tensor, mlp_out: Tensor, gate: Tensor, what: str) -> tuple[int, int, int]:
+    if z.dim() != 3:
+        raise ValueError(f"{what}: expected workspace rows [B,T,C], got {tuple(z.shape)}")
+    b, t, c = z.shape
+    _check_channels(c, what)
+    for name, u in (("dz_attn", dz_attn), ("mlp_out", mlp_out)):
+        if u.shape != z.shape:
+            raise ValueError(f"{what}: {name} {tuple(u.shape)} must match z {tuple(z.shape)}")
+    if tuple(gate.shape) != (b, c):
+        raise ValueError(f"{what}: expected gate [{b},{c}], got {tuple(gate.shape)}")
+    for u in (dz_attn, mlp_out, gate):
+        if u.dtype != z.dtype:
+            raise ValueError(f"{what}: all activations must share z's dtype {z.dtype}, got {u.dtype}")
+    return b, t, c
+
+
+def _gate_rows(gate: Tensor) -> tuple[Tensor, int]:
+    """gate and its row stride; a chunk of t6 (rows 16-byte aligned) passes without a copy."""
+    c = gate.shape[1]
+    es = gate.element_size()
+    if (gate.stride(1) == 1 and gate.stride(0) >= c and gate.stride(0) % 8 == 0 and (gate.stride(0) * es) % 16 == 0
+            and gate.data_ptr() % 16 == 0):
+        return gate, gate.stride(0)
+    return gate.contiguous(), c
+
+
+@_custom_op("branch_lazy_update")
+def branch_lazy_update(z: Tensor, dz_attn: Tensor, mlp_out: Tensor, gate: Tensor, alpha: Tensor,
+                       beta: Tensor) -> tuple[Tensor, Tensor]:
+    """(dz, z_next): dz = dz_attn + gate (.) mlp_out, z_next = z + gamma (.) dz."""
+    _require_cuda(z, dz_attn, mlp_out, gate, alpha, beta)
+    b, t, c = _branch_geom(z, dz_attn, mlp_out, gate, "branch_lazy_update")
+    _check_weight(alpha, c, "branch_lazy_update")
+    _check_weight(beta, c, "branch_lazy_update")
+    z, dz_attn, mlp_out = z.contiguous(), dz_attn.contiguous(), mlp_out.contiguous()
+    alpha, beta = alpha.contiguous(), beta.contiguous()
+    gate, gs = _gate_rows(gate)
+    dz, zn = torch.empty_like(z), torch.empty_like(z)
+    with _guard(z):
+        _lib.call("lthc_branch_lazy_fwd", z.data_ptr(), dz_attn.data_ptr(), mlp_out.data_ptr(), gate.data_ptr(), gs,
+                  alpha.data_ptr(), _code(alpha, "branch_lazy_update"), beta.data_ptr(), _code(beta, "branch_lazy_update"),
+                  dz.data_ptr(), zn.data_ptr(), b, t, c, _code(z, "branch_lazy_update"), _stream(z))
+    return dz, zn
+
+
+@branch_lazy_update.register_fake
+def _(z, dz_attn, mlp_out, gate, alpha, beta):
+    return torch.empty_like(z), torch.empty_like(z)
+
+
+@_custom_op("branch_lazy_update_bwd")
+def branch_lazy_update_bwd(grad_dz: Tensor | None, grad_z_next: Tensor, dz: Tensor, mlp_out: Tensor, gate: Tensor,
+                           alpha: Tensor, beta: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """(grad dz_attn, grad mlp_out, grad gate fp32 [B,C], grad alpha fp32, grad beta fp32)."""
+    _require_cuda(grad_z_next, dz, mlp_out, gate, alpha, beta)
+    b, t, c = _branch_geom(dz, dz, mlp_out, gate, "branch_lazy_update_bwd")
+    gz = grad_z_next.to(dz.dtype).contiguous()
+    gd = grad_dz.to(dz.dtype).contiguous() if grad_dz is not None else None
+    dz, mlp_out, alpha, beta = dz.contiguous(), mlp_out.contiguous(), alpha.contiguous(), beta.contiguous()
+    gate, gs = _gate_rows(gate)
+    g_attn, g_mlp = torch.empty_like(dz), torch.empty_like(dz)
+    g_gate = torch.empty((b, c), device=dz.device, dtype=torch.float32)
+    ga = torch.empty((c, 16), device=dz.device, dtype=torch.float32)
+    gb = torch.empty((c, 16), device=dz.device, dtype=torch.float32)
+    with _guard(dz):
+        ws_bytes = _lib.load().lthc_branch_lazy_bwd_workspace_bytes(b, t, c)
+        ws = _workspace(ws_bytes, dz.device)
+        _lib.call("lthc_branch_lazy_bwd", _p(gd), gz.data_ptr(), dz.data_ptr(), mlp_out.data_ptr(), gate.data_ptr(), gs,
+                  alpha.data_ptr(), _code(alpha, "branch_lazy_update_bwd"), beta.data_ptr(),
+                  _code(beta, "branch_lazy_update_bwd"), g_attn.data_ptr(), g_mlp.data_ptr(), g_gate.data_ptr(),
+                  ga.data_ptr(), gb.data_ptr(), ws.data_ptr(), ws_bytes, b, t, c, _code(dz, "branch_lazy_update_bwd"),
+                  _stream(dz))
+    return g_attn, g_mlp, g_gate, ga, gb
+
+
+@branch_lazy_update_bwd.register_fake
+def _(grad_dz, grad_z_next, dz, mlp_out, gate, alpha, beta):
+    b, t, c = dz.shape
+    f32 = dict(dtype=torch.float32)
+    return (torch.empty_like(dz), torch.empty_like(dz), dz.new_empty((b, c), **f32), dz.new_empty((c, 16), **f32),
+            dz.new_empty((c, 16), **f32))
+
+
+def _branch_setup(ctx, inputs, output):
+    z, dz_attn, mlp_out, gate, alpha, beta = inputs
+    dz, _ = output
+    ctx.save_for_backward(dz, mlp_out, gate, alpha, beta)
+
+
+def _branch_backward(ctx, grad_dz, grad_z_next):
+    dz, mlp_out, gate, alpha, beta = ctx.saved_tensors
+    need_z, need_attn, need_mlp, need_gate, need_a, need_b = ctx.needs_input_grad
+    if grad_z_next is None:
+        grad_z_next = torch.zeros_like(dz)
+    g_attn, g_mlp, g_gate, ga, gb = branch_lazy_update_bwd(grad_dz, grad_z_next, dz, mlp_out, gate, alpha, beta)
+    return ((grad_z_next if need_z else None), (g_attn if need_attn else None), (g_mlp if need_mlp else None),
+            (g_gate.to(gate.dtype) if need_gate else None), (ga.to(alpha.dtype) if need_a else None),
+            (gb.to(beta.dtype) if need_b else None))
+
+
+branch_lazy_update.register_autograd(_branch_backward, setup_context=_branch_setup)
+
+
+# ---------------------------------------------------------------------------
 # patch embedding fused with the shared read (tensor cores)
 # (BottleneckPatchEmbedNHWC.forward, local_thc.py:64-89, then SharedLocalRead.read,
 # :1211-1223)

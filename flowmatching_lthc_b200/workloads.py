@@ -119,6 +119,19 @@ def lazy_bytes(N: int, C: int, act_bytes: int, w_bytes: int) -> int:
     return 3 * N * C * act_bytes + 2 * C * 16 * w_bytes
 
 
+def branch_fwd_bytes(N: int, B: int, C: int, act_bytes: int, w_bytes: int) -> int:
+    """Branch epilogue + lazy update over N = B*T rows: read z, dz_attn, mlp_out,
+    write dz and z' (5 row passes; the reference's four elementwise kernels make
+    10), plus the gate rows and the weights."""
+    return 5 * N * C * act_bytes + B * C * act_bytes + 2 * C * 16 * w_bytes
+
+
+def branch_bwd_bytes(N: int, B: int, C: int, act_bytes: int, w_bytes: int) -> int:
+    """Its backward: read grad dz, grad z', dz, mlp_out, write grad dz_attn and
+    grad mlp_out; gate rows, weights and the fp32 gate / alpha / beta gradients."""
+    return 6 * N * C * act_bytes + B * C * (act_bytes + 4) + 2 * C * 16 * (w_bytes + 4)
+
+
 def final_fwd_bytes(B: int, T: int, C: int, act_bytes: int, w_bytes: int = 4) -> int:
     """Final-layer norm + modulate: read x, write m, read the norm weight and the
     image's shift / scale rows (805,318,656 + ... B at B = 64, T = 4096, C = 768)."""

@@ -224,6 +224,33 @@ LTHC_API int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const 
 LTHC_API int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int* status_dev,
                          void* stream);
 
+/* ======================= branch epilogue fused with the lazy update ========== */
+
+/* dz = dz_attn + gate (.) mlp_out   (each op rounded to the activation dtype)
+ * z_out = z + gamma (.) dz,  gamma[c] = sum_r alpha[c,r] * beta[c,r]
+ * over B images of T workspace rows [B*T, C]; gate holds one row per image
+ * (row stride gate_stride elements, e.g. a chunk of t6).  dz and z_out are
+ * written; z_out may equal z.  Replaces the end of
+ * WorkspaceSharedAdaLNBranch.forward (local_thc.py:318-323) followed by
+ * SharedReadLocalTHCSharedAdaLNJiTBlock.lazy_workspace_update (:1325-1328). */
+LTHC_API int lthc_branch_lazy_fwd(const void* z, const void* dz_attn, const void* mlp_out, const void* gate,
+                         int64_t gate_stride, const void* alpha, int alpha_dtype, const void* beta,
+                         int beta_dtype, void* dz_out, void* z_out, int64_t B, int64_t T, int64_t C,
+                         int act_dtype, void* stream);
+
+/* Backward: grad_dz (from the materialisation; may be NULL) and grad_z_out give
+ *   g_tot = grad_dz + gamma (.) grad_z_out;  grad_attn = g_tot;
+ *   grad_mlp = gate (.) g_tot;  grad_gate [B,C] = sum_rows g_tot (.) mlp_out (fp32);
+ *   grad_alpha / grad_beta [C,16] from sum_rows grad_z_out (.) dz (fp32, fixed order).
+ * grad_gate, grad_alpha and grad_beta may be NULL.  The grad of z is grad_z_out. */
+LTHC_API size_t lthc_branch_lazy_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C);
+LTHC_API int lthc_branch_lazy_bwd(const void* grad_dz, const void* grad_z_out, const void* dz,
+                         const void* mlp_out, const void* gate, int64_t gate_stride,
+                         const void* alpha, int alpha_dtype, const void* beta, int beta_dtype,
+                         void* grad_attn, void* grad_mlp, float* grad_gate, float* grad_alpha,
+                         float* grad_beta, void* workspace, size_t workspace_bytes, int64_t B,
+                         int64_t T, int64_t C, int act_dtype, void* stream);
+
 /* ======================= patch embedding fused with the shared read ========= */
 
 /* X0 = NHWC(conv1x1(conv4x4/4(img; w1); w2) + b2) and Z = read(X0; alpha) in one

@@ -20,6 +20,9 @@
  *   oracle_final_fwd       FinalLayerSharedAdaLN.forward     local_thc.py:865-873 (RMSNorm
  *                          jit_shared_adaln.py:20-30, modulate local_thc.py:37-38), without its Linear
  *   oracle_final_bwd       autograd of the line above
+ *   oracle_branch_fwd      WorkspaceSharedAdaLNBranch.forward's output sum   local_thc.py:318-323,
+ *                          then lazy_workspace_update                        :1325-1328
+ *   oracle_branch_bwd      autograd of the two lines above
  *
  * Arithmetic: inputs are widened to fp32 exactly; per-element sums over the 16
  * cell positions or the L layers accumulate in fp32 with fused multiply-add in
@@ -369,4 +372,58 @@ void oracle_final_bwd(const void* x, const void* w, int wdt, const void* scale, 
     if (gw) gw[c] = (float)aw;
   }
   free(rs);
+}
+
+/* ---- branch epilogue + lazy update --------------------------------------------
+ * WorkspaceSharedAdaLNBranch.forward's last lines (local_thc.py:318-323):
+ *   dz = dz_attn + gate * mlp_out     (the product and the sum each rounded)
+ * then lazy_workspace_update (:1325-1328): z' = z + gamma * dz (fmaf, one rounding).
+ * Rows n of B images of T rows; gate rows of stride gs. */
+void oracle_branch_fwd(const void* z, const void* attn, const void* mlp, const void* gate, int64_t gs, const void* a,
+                       int adt, const void* b, int bdt, void* dz_out, void* z_out, int64_t B, int64_t T, int64_t C,
+                       int dt) {
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < B * T; ++n) {
+    int64_t img = n / T;
+    for (int64_t c = 0; c < C; ++c) {
+      float g = gamma_of(a, adt, b, bdt, c);
+      float gm = rnd(ld(gate, dt, img * gs + c) * ld(mlp, dt, n * C + c), dt);
+      float dz = rnd(ld(attn, dt, n * C + c) + gm, dt);
+      st(dz_out, dt, n * C + c, dz);
+      st(z_out, dt, n * C + c, fmaf(g, dz, ld(z, dt, n * C + c)));
+    }
+  }
+}
+
+/* Its autograd: g_tot = g_dz + round(gamma * g_zo); grad_attn = g_tot;
+ * grad_mlp = round(gate * g_tot); grad_gate[b] = sum_rows round(g_tot * mlp);
+ * ggamma = sum_rows g_zo * dz; grad_a = ggamma * b, grad_b = ggamma * a (fp64 sums). */
+void oracle_branch_bwd(const void* g_dz, const void* g_zo, const void* dz, const void* mlp, const void* gate,
+                       int64_t gs, const void* a, int adt, const void* b, int bdt, void* g_attn, void* g_mlp,
+                       float* g_gate, float* ga, float* gb, int64_t B, int64_t T, int64_t C, int dt) {
+#pragma omp parallel for schedule(static)
+  for (int64_t c = 0; c < C; ++c) {
+    float g = gamma_of(a, adt, b, bdt, c);
+    double gam = 0.0;
+    for (int64_t img = 0; img < B; ++img) {
+      double gg = 0.0;
+      float gt = ld(gate, dt, img * gs + c);
+      for (int64_t t = 0; t < T; ++t) {
+        int64_t i = (img * T + t) * C + c;
+        float zo = ld(g_zo, dt, i);
+        float from_lazy = rnd(g * zo, dt);
+        float tot = g_dz ? rnd(ld(g_dz, dt, i) + from_lazy, dt) : from_lazy;
+        st(g_attn, dt, i, tot);
+        st(g_mlp, dt, i, gt * tot);
+        gg += (double)rnd(tot * ld(mlp, dt, i), dt);
+        gam += (double)zo * (double)ld(dz, dt, i);
+      }
+      if (g_gate) g_gate[img * C + c] = (float)gg;
+    }
+    float s = (float)gam;
+    for (int r = 0; r < 16; ++r) {
+      if (ga) ga[c * 16 + r] = s * ld(b, bdt, c * 16 + r);
+      if (gb) gb[c * 16 + r] = s * ld(a, adt, c * 16 + r);
+    }
+  }
 }

@@ -38,6 +38,8 @@ def lib() -> ctypes.CDLL:
             "oracle_lazy_bwd": [p, p, p, i, p, i, p, p, p, i64, i64, i],
             "oracle_final_fwd": [p, p, i, p, p, i64, p, i64, i64, i64, c_float, i],
             "oracle_final_bwd": [p, p, i, p, i64, p, p, p, p, p, i64, i64, i64, c_float, i],
+            "oracle_branch_fwd": [p, p, p, p, i64, p, i, p, i, p, p, i64, i64, i64, i],
+            "oracle_branch_bwd": [p, p, p, p, p, i64, p, i, p, i, p, p, p, p, p, i64, i64, i64, i],
             "oracle_num_threads": [],
             "oracle_set_num_threads": [i],
         }
@@ -209,5 +211,31 @@ def final_bwd(grad_out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, sca
     return gx, gw, gsh, gsc
 
 
+def branch_fwd(z, dz_attn, mlp_out, gate, alpha, beta):
+    """WorkspaceSharedAdaLNBranch's output sum (local_thc.py:318-323) then the lazy
+    update (:1325-1328): (dz, z').  z, dz_attn, mlp_out [B,T,C]; gate [B,C]."""
+    z, dz_attn, mlp_out, gate, alpha, beta = (_c(t) for t in (z, dz_attn, mlp_out, gate, alpha, beta))
+    b, t, c = z.shape
+    dz, zo = torch.empty_like(z), torch.empty_like(z)
+    lib().oracle_branch_fwd(_p(z), _p(dz_attn), _p(mlp_out), _p(gate), c, _p(alpha), _DT[alpha.dtype], _p(beta),
+                            _DT[beta.dtype], _p(dz), _p(zo), b, t, c, _DT[z.dtype])
+    return dz, zo
+
+
+def branch_bwd(g_dz, g_zo, dz, mlp_out, gate, alpha, beta):
+    """Autograd of branch_fwd: (grad dz_attn, grad mlp_out, grad gate fp32 [B,C],
+    grad alpha fp32, grad beta fp32); g_dz may be None."""
+    g_zo, dz, mlp_out, gate, alpha, beta = (_c(t) for t in (g_zo, dz, mlp_out, gate, alpha, beta))
+    g_dz = _c(g_dz) if g_dz is not None else None
+    b, t, c = dz.shape
+    g_attn, g_mlp = torch.empty_like(dz), torch.empty_like(dz)
+    g_gate = torch.empty(b, c, dtype=torch.float32)
+    ga, gb = torch.empty(c, 16, dtype=torch.float32), torch.empty(c, 16, dtype=torch.float32)
+    lib().oracle_branch_bwd(_p(g_dz), _p(g_zo), _p(dz), _p(mlp_out), _p(gate), c, _p(alpha), _DT[alpha.dtype],
+                            _p(beta), _DT[beta.dtype], _p(g_attn), _p(g_mlp), _p(g_gate), _p(ga), _p(gb), b, t, c,
+                            _DT[dz.dtype])
+    return g_attn, g_mlp, g_gate, ga, gb
+
+
 __all__ = ["lib", "num_threads", "set_num_threads", "read", "write", "write_add", "materialise", "materialise_bwd",
-           "weight_grad", "lazy_fwd", "lazy_bwd", "final_fwd", "final_bwd", "OUT"]
+           "weight_grad", "lazy_fwd", "lazy_bwd", "final_fwd", "final_bwd", "branch_fwd", "branch_bwd", "OUT"]

@@ -3,7 +3,7 @@ reference's own eager PyTorch code (tongtongliang/flowmatching_lthc) on CPU.
 
 Run from the repository root with the reference importable, e.g.
 
-    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py [all|lthc|final]
+    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py [all|lthc|final|branch]
 
 The reference is only needed to (re)generate the fixtures; the committed ``*.pt``
 files are what the tests read.  Every tensor is produced by the reference
@@ -14,6 +14,8 @@ functions named below (paths inside the reference repository):
   LayerLocalWrite.gamma_from_alpha       flowmatching_lthc/models/local_thc.py:1278-1283
   Block.lazy_workspace_update            flowmatching_lthc/models/local_thc.py:1325-1328
   Model.final_accumulate_reference       flowmatching_lthc/models/local_thc.py:1368-1372
+  WorkspaceSharedAdaLNBranch.forward (output epilogue), Block.branch_update
+                                         flowmatching_lthc/models/local_thc.py:318-323, 1322-1323
   FinalLayerSharedAdaLN (norm_final = RMSNorm, modulate, linear)
                                          flowmatching_lthc/models/local_thc.py:37-38, 865-873
                                          flowmatching_lthc/models/jit_shared_adaln.py:20-30
@@ -142,6 +144,70 @@ def make_final_case(name: str, *, B: int, T: int, C: int, dtype: torch.dtype, se
     return out
 
 
+class _Fixed(torch.nn.Module):
+    """Stands in for the branch's attention or MLP: returns a fixed leaf tensor so
+    the epilogue's inputs (and their gradients) are observable."""
+
+    def __init__(self, value: torch.Tensor) -> None:
+        super().__init__()
+        self.value = value
+
+    def forward(self, *args):
+        return self.value
+
+
+def make_branch_case(name: str, *, B: int, G: int, C: int, dtype: torch.dtype, seed: int) -> dict:
+    """WorkspaceSharedAdaLNBranch.forward's output epilogue (gate product and sum)
+    followed by Block.lazy_workspace_update, through the reference's own
+    branch_update / lazy_workspace_update with the attention and the MLP replaced
+    by fixed leaves A and M and gate_msa = 1, so that dz_attn = A exactly:
+        dz = A + gate_mlp (.) M,   z' = z + gamma (.) dz."""
+    gen = torch.Generator().manual_seed(seed)
+
+    def randn(*shape, mean=0.0, std=1.0):
+        return torch.randn(*shape, generator=gen) * std + mean
+
+    T, hi = G * G, 4 * G
+    z = randn(B, T, C).to(dtype)
+    A = randn(B, T, C, std=0.5).to(dtype)
+    M = randn(B, T, C).to(dtype)
+    t6 = randn(B, 6 * C, std=0.5)
+    t6[:, 2 * C:3 * C] = 1.0  # gate_msa
+    t6 = t6.to(dtype)
+    R = randn(C, 16, mean=1.0 / 16, std=0.01)
+    P = randn(C, 16, std=0.02)
+    g_dz = randn(B, T, C).to(dtype)
+    g_zn = randn(B, T, C).to(dtype)
+
+    read = L.SharedLocalRead(hi, G, C, C, use_softmax_write=False)
+    read.read_logits.data.copy_(R)
+    block = L.SharedReadLocalTHCSharedAdaLNJiTBlock(C, num_heads=C // 8, high_grid=hi, workspace_grid=G)
+    block.write.write_weight.data.copy_(P)
+    block.branch.to(dtype)
+    Ar, Mr = A.clone().requires_grad_(True), M.clone().requires_grad_(True)
+    block.branch.attn, block.branch.mlp = _Fixed(Ar), _Fixed(Mr)
+    zr, t6r = z.clone().requires_grad_(True), t6.clone().requires_grad_(True)
+    dz = block.branch_update(zr, t6r, None)
+    zn = block.lazy_workspace_update(zr, dz, read)
+    leaves = (zr, Ar, Mr, t6r, read.read_logits, block.write.write_weight)
+    g_both = torch.autograd.grad((dz, zn), leaves, (g_dz, g_zn), retain_graph=True)
+    g_lazy = torch.autograd.grad(zn, leaves, g_zn)
+    out: dict = {"meta": {"name": name, "B": B, "G": G, "C": C, "dtype": str(dtype), "seed": seed},
+                 "z": z, "dz_attn": A, "mlp_out": M, "gate": t6[:, 5 * C:].contiguous(), "R": R, "P": P,
+                 "g_dz": g_dz, "g_zn": g_zn, "dz": dz.detach(), "z_next": zn.detach()}
+    for tag, g in (("both", g_both), ("lazy_only", g_lazy)):
+        gz, gA, gM, gt6, gR, gP = g
+        out.update({f"{tag}_gz": gz, f"{tag}_gattn": gA, f"{tag}_gmlp": gM,
+                    f"{tag}_ggate": gt6[:, 5 * C:].contiguous(), f"{tag}_gR": gR, f"{tag}_gP": gP})
+    return out
+
+
+BRANCH_CASES = [
+    ("branch_g4_c768_bf16", dict(B=2, G=4, C=768, dtype=torch.bfloat16, seed=20)),
+    ("branch_g4_c40_f32", dict(B=3, G=4, C=40, dtype=torch.float32, seed=21)),
+    ("branch_g4_c64_f16", dict(B=2, G=4, C=64, dtype=torch.float16, seed=22)),
+]
+
 FINAL_CASES = [
     ("final_t64_c768_bf16", dict(B=2, T=64, C=768, dtype=torch.bfloat16, seed=10)),
     ("final_t16_c40_f32", dict(B=3, T=16, C=40, dtype=torch.float32, seed=11)),
@@ -162,6 +228,8 @@ def main(which: str = "all") -> None:
         jobs += [(name, make_case, kw) for name, kw in CASES]
     if which in ("all", "final"):
         jobs += [(name, make_final_case, kw) for name, kw in FINAL_CASES]
+    if which in ("all", "branch"):
+        jobs += [(name, make_branch_case, kw) for name, kw in BRANCH_CASES]
     for name, fn, kw in jobs:
         case = fn(name, **kw)
         path = HERE / f"{name}.pt"

@@ -57,6 +57,15 @@ P = 256  # a 16-byte aligned non-null address that is never dereferenced
     (lambda L: L.lthc_final_norm_modulate_fwd(P, None, 0, P, P, 1536, P, 2, 4096, 768, 1e-6, 1, None), 1),
     (lambda L: L.lthc_final_norm_modulate_bwd(P, P, 0, P, 1536, P, None, None, None, None, P, 1 << 30, 2, 4096, 768,
                                               1e-6, 1, None), 1),
+    (lambda L: L.lthc_branch_lazy_fwd(P, P, P, P, 4608, P, 0, P, 0, P, P, 2, 256, 770, 1, None), 2),
+    (lambda L: L.lthc_branch_lazy_fwd(P, P, P, P, 700, P, 0, P, 0, P, P, 2, 256, 768, 1, None), 2),
+    (lambda L: L.lthc_branch_lazy_fwd(P, P, P, P, 4608, P, 0, P, 6, P, P, 2, 256, 768, 1, None), 3),
+    (lambda L: L.lthc_branch_lazy_fwd(P, P, P + 4, P, 4608, P, 0, P, 0, P, P, 2, 256, 768, 1, None), 4),
+    (lambda L: L.lthc_branch_lazy_fwd(P, None, P, P, 4608, P, 0, P, 0, P, P, 2, 256, 768, 1, None), 1),
+    (lambda L: L.lthc_branch_lazy_bwd(None, None, P, P, P, 4608, P, 0, P, 0, P, P, P, P, P, P, 1 << 30, 2, 256, 768,
+                                      1, None), 1),
+    (lambda L: L.lthc_branch_lazy_bwd(P, P, P, P, P, 4612, P, 0, P, 0, P, P, P, P, P, P, 1 << 30, 2, 256, 768, 1,
+                                      None), 2),
 ])
 def test_validation_errors(call, status):
     lib = _lib.load()
@@ -74,6 +83,9 @@ def test_empty_batch_is_a_successful_no_op():
     assert lib.lthc_final_norm_modulate_fwd(P, P, 0, P, P, 1536, P, 0, 4096, 768, 1e-6, 1, None) == 0
     assert lib.lthc_final_norm_modulate_bwd(P, P, 0, P, 1536, P, P, None, None, None, None, 0, 0, 4096, 768, 1e-6, 1,
                                             None) == 0
+    assert lib.lthc_branch_lazy_fwd(P, P, P, P, 4608, P, 0, P, 0, P, P, 0, 256, 768, 1, None) == 0
+    assert lib.lthc_branch_lazy_bwd(None, P, P, P, P, 4608, P, 0, P, 0, P, P, None, None, None, None, 0, 2, 0, 768, 1,
+                                    None) == 0
 
 
 def test_workspace_queries():
@@ -88,6 +100,9 @@ def test_workspace_queries():
     assert lib.lthc_final_norm_modulate_bwd_workspace_bytes(0, 4096, 768) == 0
     nf = lib.lthc_final_norm_modulate_bwd_workspace_bytes(64, 4096, 768)
     assert nf > 0 and nf % (64 * 3 * 768 * 4) == 0
+    assert lib.lthc_branch_lazy_bwd_workspace_bytes(0, 256, 768) == 0
+    nb = lib.lthc_branch_lazy_bwd_workspace_bytes(64, 256, 768)
+    assert nb > 0 and nb % (64 * 2 * 768 * 4) == 0
 
 
 def test_call_helper_raises_with_message():

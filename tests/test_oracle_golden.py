@@ -187,3 +187,59 @@ def test_final_norm_modulate_backward(final_case):
     # shift / scale gradients are sums over tokens, rounded once to the parameter dtype
     assert rel_err(gsh.to(dt), c["g_shift"]) < TOL[dt]
     assert rel_err(gsc.to(dt), c["g_scale"]) < TOL[dt]
+
+
+# ---- branch epilogue fused with the lazy update --------------------------------
+# (WorkspaceSharedAdaLNBranch.forward's output sum, then lazy_workspace_update)
+BRANCH_CASES = ["branch_g4_c768_bf16", "branch_g4_c40_f32", "branch_g4_c64_f16"]
+BRANCH_TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 5e-3}
+
+
+@pytest.fixture(scope="module", params=BRANCH_CASES)
+def branch_case(request):
+    return torch.load(GOLDEN / f"{request.param}.pt")
+
+
+def test_branch_lazy_forward(branch_case):
+    """dz is the reference's op-by-op sum bit for bit (one rounding per op, as
+    torch rounds); z' differs from the reference's z + gamma*dz only by gamma kept
+    in fp32 and one rounding of the fused multiply-add."""
+    c = branch_case
+    dt = c["z"].dtype
+    dz, zn = O.branch_fwd(c["z"], c["dz_attn"], c["mlp_out"], c["gate"], c["R"].to(dt), c["P"].to(dt))
+    assert torch.equal(dz, c["dz"])
+    assert rel_err(zn, c["z_next"]) < BRANCH_TOL[dt]
+    assert exact_fraction(zn, c["z_next"]) > 0.98
+    # the same as the unfused lazy update applied to that dz
+    assert torch.equal(zn, O.lazy_fwd(c["z"], dz, c["R"].to(dt), c["P"].to(dt)))
+
+
+@pytest.mark.parametrize("tag", ["both", "lazy_only"])
+def test_branch_lazy_backward(branch_case, tag):
+    c = branch_case
+    dt = c["z"].dtype
+    tol = BRANCH_TOL[dt]
+    g_dz = c["g_dz"] if tag == "both" else None
+    g_attn, g_mlp, g_gate, ga, gb = O.branch_bwd(g_dz, c["g_zn"], c["dz"], c["mlp_out"], c["gate"], c["R"].to(dt),
+                                                 c["P"].to(dt))
+    assert rel_err(g_attn, c[f"{tag}_gattn"]) < tol
+    assert rel_err(g_mlp, c[f"{tag}_gmlp"]) < tol
+    assert rel_err(g_gate.to(dt), c[f"{tag}_ggate"]) < tol
+    assert rel_err(ga, c[f"{tag}_gR"]) < tol
+    assert rel_err(gb, c[f"{tag}_gP"]) < tol
+    assert torch.equal(c[f"{tag}_gz"], c["g_zn"])  # identity branch of the recurrence
+    if tag == "both":  # gamma's rounding only enters through gamma * g_zn, small beside g_dz
+        assert exact_fraction(g_attn, c[f"{tag}_gattn"]) > 0.98
+
+
+def test_branch_lazy_empty_and_single_row():
+    for b, t in ((0, 16), (2, 0), (1, 1)):
+        z = torch.randn(b, t, 16)
+        gate = torch.randn(b, 16)
+        a, p = torch.rand(16, 16), torch.randn(16, 16)
+        dz, zn = O.branch_fwd(z, z * 0.5, z * 2, gate, a, p)
+        assert dz.shape == z.shape and zn.shape == z.shape
+        g_attn, g_mlp, g_gate, ga, gb = O.branch_bwd(None, z, dz, z, gate, a, p)
+        assert g_gate.shape == (b, 16)
+        if b * t == 0:
+            assert torch.count_nonzero(ga) == 0 and torch.count_nonzero(g_gate) == 0
