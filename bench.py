@@ -219,10 +219,11 @@ def op_step(op: str, cfg: dict):
         attn = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
         mlp = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
         gate = (0.5 * torch.randn(B, 6 * C, device=x0.device, generator=gen)).to(torch.bfloat16).chunk(6, dim=-1)[5]
+        gdz = torch.randn(B, G * G, C, device=x0.device, generator=gen).to(torch.bfloat16)
         n = B * G * G
         table["branch_fwd"] = (lambda: ops.call(ops.branch_lazy_update, z, attn, mlp, gate, alpha, beta),
                                W.branch_fwd_bytes(n, B, C, 2, 2), 1, "branch_lazy_fwd_kernel<bf16>")
-        table["branch_bwd"] = (lambda: ops.call(ops.branch_lazy_update_bwd, attn, z, mlp, attn, gate, alpha, beta),
+        table["branch_bwd"] = (lambda: ops.call(ops.branch_lazy_update_bwd, gdz, z, attn, mlp, gate, alpha, beta),
                                W.branch_bwd_bytes(n, B, C, 2, 2), 2,
                                "branch_lazy_bwd_kernel<bf16> + branch_lazy_bwd_finalize_kernel")
     if op in ("final_fwd", "final_bwd"):

@@ -421,10 +421,15 @@ int check_weight_dtype(int dt, const char* name) {
 // Backward CTAs per image (each owns a contiguous row range of one image); a
 // pure function of the shape and the SM count, so that the workspace query and
 // the launch agree.
+// CTAs per image of the branch backward (each owns a contiguous row range of one
+// image): close to two full waves of its two resident CTAs per SM, counted with
+// the 16-bit slice width (the same count for every dtype, so the workspace
+// query needs no dtype).
 int64_t branch_ctas_per_image(int64_t B, int64_t T, int64_t C, int sms) {
   if (B <= 0 || T <= 0) return 1;
-  const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(sms) * 4 / lazy_slices(C, 4));
-  const int64_t k = std::max<int64_t>(1, std::min<int64_t>(ceil_div(target, B), ceil_div(T, kLazyWarps)));
+  const int64_t slots = 2 * static_cast<int64_t>(sms);
+  const int64_t k = std::max<int64_t>(1, std::min<int64_t>(2 * slots / (B * lazy_slices(C, 2)),
+                                                           ceil_div(T, kLazyWarps)));
   return ceil_div(T, ceil_div(T, k));
 }
 

@@ -214,11 +214,12 @@ __global__ void __launch_bounds__(256) lazy_bwd_kernel(const __grid_constant__ L
 
 // ggamma[c] = sum_k partial[k * kstride + c];  grad_a[c,r] = ggamma*b[c,r];
 // grad_b[c,r] = ggamma*a[c,r].  One block per 32 channels: warp w sums the
-// partials k = w, w + 8, ... (coalesced over the channels, eight independent
-// chains instead of one chain of nblk dependent adds), the eight warp sums are
-// added in warp order, then the block writes its 32 x 16 outputs.  Fixed order:
-// bitwise reproducible.
-constexpr int kGammaFinalizeWarps = 8;
+// partials k = w, w + 16, ... (coalesced over the channels, sixteen chains of
+// eight loads in flight instead of one chain of nblk dependent adds), the warp
+// sums are added in warp order, then the block writes its 32 x 16 outputs.
+// Fixed order: bitwise reproducible.
+constexpr int kGammaFinalizeWarps = 16;
+constexpr int kColumnBatch = 8;  // independent partial loads in flight per warp
 
 // Fixed-order column sums of 32 channels c0 .. c0+31 over nblk partial rows
 // (row k at partial + k * kstride) by a block of kGammaFinalizeWarps warps; the
@@ -232,12 +233,12 @@ __device__ __forceinline__ void column_sum32(const float* __restrict__ partial, 
   float s = 0.f;
   if (c < C) {
     int64_t k = warp;
-    for (; k + 3 * kGammaFinalizeWarps < nblk; k += 4 * kGammaFinalizeWarps) {
-      const float v0 = partial[k * kstride + c];
-      const float v1 = partial[(k + kGammaFinalizeWarps) * kstride + c];
-      const float v2 = partial[(k + 2 * kGammaFinalizeWarps) * kstride + c];
-      const float v3 = partial[(k + 3 * kGammaFinalizeWarps) * kstride + c];
-      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v0), v1), v2), v3);
+    for (; k + (kColumnBatch - 1) * kGammaFinalizeWarps < nblk; k += kColumnBatch * kGammaFinalizeWarps) {
+      float v[kColumnBatch];
+#pragma unroll
+      for (int j = 0; j < kColumnBatch; ++j) v[j] = partial[(k + j * kGammaFinalizeWarps) * kstride + c];
+#pragma unroll
+      for (int j = 0; j < kColumnBatch; ++j) s = __fadd_rn(s, v[j]);
     }
     for (; k < nblk; k += kGammaFinalizeWarps) s = __fadd_rn(s, partial[k * kstride + c]);
   }
