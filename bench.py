@@ -226,6 +226,14 @@ def op_step(op: str, cfg: dict):
         table["branch_bwd"] = (lambda: ops.call(ops.branch_lazy_update_bwd, gdz, z, attn, mlp, gate, alpha, beta),
                                W.branch_bwd_bytes(n, B, C, 2, 2), 2,
                                "branch_lazy_bwd_kernel<bf16> + branch_lazy_bwd_finalize_kernel")
+    if op == "materialise_final_fwd":
+        # inference: materialisation + final RMSNorm + modulate in one pass (m written, X_L not)
+        nw = torch.ones(C, device=x0.device) + 0.1 * torch.randn(C, device=x0.device)
+        t2 = (0.5 * torch.randn(B, 2 * C, device=x0.device)).to(torch.bfloat16)
+        sh, sc = t2.chunk(2, dim=1)
+        table["materialise_final_fwd"] = (
+            lambda: ops.call(ops.materialise_final, x0, dz, P, nw, sh, sc, 1e-6),
+            W.materialise_bytes(B, G, C, L, 2) + 4 * C + 2 * 2 * B * C, 1, "materialise_final_kernel<bf16, 12> (clusters)")
     if op in ("final_fwd", "final_bwd"):
         # final-layer prologue on the materialised residual [B, 4096, 768] (FinalLayerSharedAdaLN)
         T = 16 * G * G
@@ -241,7 +249,7 @@ def op_step(op: str, cfg: dict):
 
 
 OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
-       "final_fwd", "final_bwd", "embed_fwd", "branch_fwd", "branch_bwd")
+       "final_fwd", "final_bwd", "embed_fwd", "branch_fwd", "branch_bwd", "materialise_final_fwd")
 MODEL_OPS = ("model_fwd", "train_step", "sample")
 # Largest batch per model call for which the reference Triton materialisation's
 # 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
@@ -422,6 +430,7 @@ WORKLOADS = {
     "lazy_bwd": "lazy update bwd, config 2 shapes",
     "final_fwd": "final-layer RMSNorm + AdaLN modulate on X_L [B, 4096, 768], config 2 shapes",
     "final_bwd": "final-layer RMSNorm + modulate bwd (grad X_L, grad norm weight / shift / scale), config 2 shapes",
+    "materialise_final_fwd": "materialisation fused with the final RMSNorm + modulate (inference), config 2 shapes",
     "branch_fwd": "branch output sum (dz_attn + gate*mlp_out) fused with the lazy update, config 2 workspace shapes",
     "branch_bwd": "its backward (grad dz_attn / mlp_out / gate / alpha / beta), config 2 workspace shapes",
     "embed_fwd": "patch embedding (4x4 conv 3->128, 1x1 conv 128->768) + shared read, config 3 images, tcgen05",
