@@ -588,6 +588,8 @@ def main() -> int:
     if extras:
         line["kernels"] = extras.get("kernels")
         line["comparators"] = extras.get("comparators")
+        if "materialise_final_clusters" in extras:
+            line["materialise_final_clusters"] = extras["materialise_final_clusters"]
     if r.is_main and r.world == 1 and args.op == "materialise_fwd":
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if r.is_main:
@@ -601,6 +603,8 @@ def measure_kernels(cfg: dict, stream, peak) -> dict:
     """Device-timed GB/s of every LTHC op at B=64 bf16 (informational; not the
     headline), plus the reference's Triton ops on the same inputs when the
     reference package is installed under baseline/_ref."""
+    from flowmatching_lthc_b200 import ops
+
     out: dict = {"kernels": {}, "comparators": {}}
     iters = 20
     for op in OPS:
@@ -634,6 +638,8 @@ def measure_kernels(cfg: dict, stream, peak) -> dict:
         except Exception as e:  # capture is an extra measurement, not the headline
             graph_ms = f"capture failed: {type(e).__name__}"
         best = min(ms, graph_ms) if isinstance(graph_ms, float) else ms
+        if op == "materialise_final_fwd":
+            out["materialise_final_clusters"] = ops.materialise_final_clusters(cfg["x0"], L)
         out["kernels"][op] = {"ms": round(ms, 4), "gbs": round(nbytes / (best / 1e3) / 1e9, 1),
                               "frac": round(nbytes / (best / 1e3) / 1e9 / peak, 4), "bytes": nbytes,
                               "launches": launches, "eager_ms": round(ms, 4),

@@ -1372,16 +1372,16 @@ int lthc_materialise_final_fwd(const void* x0, const void* const* dz, const void
                   m_out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream), false, nullptr);
 }
 
-int lthc_materialise_final_supported(int64_t C, int n_layers, int act_dtype, int* supported) {
-  if (!supported) return fail(LTHC_ERR_NULL_POINTER, "supported is NULL");
-  *supported = 0;
+int lthc_materialise_final_supported(int64_t C, int n_layers, int act_dtype, int* clusters) {
+  if (!clusters) return fail(LTHC_ERR_NULL_POINTER, "clusters is NULL");
+  *clusters = 0;
   LTHC_TRY(check_matfinal(1, 16, C, n_layers, act_dtype, LTHC_DTYPE_F32, LTHC_DTYPE_F32, C, 0.f));
   int sms = 0;
   LTHC_TRY(current_device(&sms));
   int cap = 0;
   LTHC_TRY(matfinal(nullptr, nullptr, nullptr, LTHC_DTYPE_F32, n_layers, nullptr, LTHC_DTYPE_F32, nullptr, nullptr, C,
                     0.f, nullptr, 1, 16, C, act_dtype, nullptr, true, &cap));
-  *supported = cap > 0 ? 1 : 0;
+  *clusters = cap;
   return LTHC_OK;
 }
 

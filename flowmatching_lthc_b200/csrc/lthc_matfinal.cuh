@@ -15,9 +15,9 @@
 // slice's partial sum of squares per token and pushes the 16 sums into a slot of
 // every cluster peer's shared memory (st.async, completion counted in bytes on the
 // peer's mbarrier).  Once a CTA holds the partials of every slice it adds them in
-// slice order (so every CTA derives the same rstd), releases the slot to all
-// senders with remote mbarrier arrivals, applies the norm and the modulation to
-// its 64 channels and stores the m tile with TMA.  Every wait is a bounded
+// slice order (so every CTA derives the same rstd), applies the norm and the
+// modulation to its 64 channels, stores the m tile with TMA and releases the
+// slot to all senders with one remote mbarrier arrival each.  Every wait is a bounded
 // mbarrier wait (2 s, then the device error word is set and the kernel returns).
 #pragma once
 
@@ -60,36 +60,34 @@ __device__ __forceinline__ void mbar_remote_arrive(uint32_t rbar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(rbar) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait with cluster-scope acquire (the phase is completed by other CTAs).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  unsigned long long limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - t0 > limit_ns) {
-      atomicExch(&g_device_error, 1);
-      return false;
-    }
-  }
-}
-
 // ---- kernel ----------------------------------------------------------------------
 constexpr int kMatFinalMaxSlices = 16;      // C <= 1024: a cluster of at most 16 CTAs
-constexpr int kMatFinalXSlots = 2;          // exchange slots (strips whose partials can be in flight)
 constexpr int kStripTokens = 4 * kBoxCols;  // tokens of one strip (4 rows x 16 columns)
+
+// Pipeline.  The load ring (kStages stages of X_0 + L update tiles) only feeds
+// phase A, which rounds X_L into a separate ring of kRing output tiles and hands
+// the load stage straight back, so every load stage stays available for
+// prefetching.  Phase B of a strip runs kLook iterations after its phase A (its
+// partials cross the cluster meanwhile); its output tile is stored by TMA and
+// reused once at most kStoreLag newer stores are still reading it, which needs
+// kRing >= kLook + kStoreLag + 2.  kXSlots exchange slots hold the partials of
+// the strips between their phase A and their phase B.
+#ifndef LTHC_MATFINAL_STAGES_16BIT
+#define LTHC_MATFINAL_STAGES_16BIT 4
+#endif
+#ifndef LTHC_MATFINAL_LOOK_16BIT
+#define LTHC_MATFINAL_LOOK_16BIT 2
+#endif
+template <typename T, int LT>
+struct MatFinalPipe {
+  static constexpr bool k16 = sizeof(T) == 2;
+  static constexpr int kStages = k16 ? LTHC_MATFINAL_STAGES_16BIT : 2;
+  static constexpr int kLook = k16 ? LTHC_MATFINAL_LOOK_16BIT : 1;
+  static constexpr int kStoreLag = 1;
+  static constexpr int kRing = kLook + kStoreLag + 2;
+  static constexpr int kXSlots = kLook + 1;
+  static constexpr int kMinBlocks = k16 ? 2 : 1;
+};
 
 struct MatFinalParams {
   BcastTmaParams m;       // tm_base = X_0, tm_dz / w = the updates and betas, tm_out = m
@@ -105,14 +103,19 @@ struct MatFinalParams {
 template <typename T, int LT>
 struct MatFinalLayout {
   using Base = BcastLayout<T, LT, true>;
-  static constexpr int kStages = Base::kStages;
-  static constexpr int kStageBytes = Base::kStageBytes;
-  static constexpr int kRecvOffset = kStages * kStageBytes;
-  static constexpr int kRecvBytes = kMatFinalXSlots * kMatFinalMaxSlices * kStripTokens * 4;
+  using Pipe = MatFinalPipe<T, LT>;
+  static constexpr int kStages = Pipe::kStages;
+  static constexpr int kRing = Pipe::kRing;
+  static constexpr int kXSlots = Pipe::kXSlots;
+  static constexpr int kStageBytes = Base::kStageBytes;  // X_0 tile + L update tiles
+  static constexpr int kTileBytes = Base::kBaseBytes;    // one X_L / m tile
+  static constexpr int kRingOffset = kStages * kStageBytes;
+  static constexpr int kRecvOffset = kRingOffset + kRing * kTileBytes;
+  static constexpr int kRecvBytes = kXSlots * kMatFinalMaxSlices * kStripTokens * 4;
   static constexpr int kBarrierOffset = kRecvOffset + kRecvBytes;
-  static constexpr int kSmemBytes = kBarrierOffset + (2 * kStages + 2 * kMatFinalXSlots) * 8 + 128;
-  static_assert(kStageBytes % 16 == 0 && kRecvOffset % 16 == 0, "16-byte aligned regions");
-  static_assert(2 * kSmemBytes <= 226 * 1024, "two CTAs per SM");
+  static constexpr int kSmemBytes = kBarrierOffset + (2 * kStages + 2 * kXSlots) * 8 + 128;
+  static_assert(kStageBytes % 128 == 0 && kTileBytes % 128 == 0, "128-byte aligned tiles");
+  static_assert(Pipe::kMinBlocks * (kSmemBytes + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
 };
 
 // Sum of v[0..15] over the 32 lanes, scattered: afterwards lanes 2t and 2t + 1
@@ -155,7 +158,7 @@ __device__ __forceinline__ void sts_raw(uint32_t addr, typename Pair<T>::R v) {
 }
 
 template <typename T, int LT>
-__global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
+__global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, MatFinalPipe<T, LT>::kMinBlocks)
     materialise_final_kernel(const __grid_constant__ MatFinalParams q) {
   constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
   using Lay = MatFinalLayout<T, LT>;
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarrierOffset);
   uint64_t* empty = full + Lay::kStages;
   uint64_t* xfull = empty + Lay::kStages;
-  uint64_t* xempty = xfull + kMatFinalXSlots;
+  uint64_t* xempty = xfull + Lay::kXSlots;
   float* recv = reinterpret_cast<float*>(smem + Lay::kRecvOffset);  // [slot][slice][token]
 
   const int warp = threadIdx.x >> 5;
@@ -185,11 +188,11 @@ __global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < Lay::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], Shape::kConsumerWarps);  // each consumer warp, once phase A has read the stage
     }
-    for (int x = 0; x < kMatFinalXSlots; ++x) {
+    for (int x = 0; x < Lay::kXSlots; ++x) {
       mbar_init(&xfull[x], 1);                             // + the peers' bytes
-      mbar_init(&xempty[x], nsl * Shape::kConsumerWarps);  // every consumer warp of the cluster
+      mbar_init(&xempty[x], nsl);  // one release from every CTA of the cluster
     }
     fence_barrier_init();
   }
@@ -232,6 +235,15 @@ __global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
   }
 
   // ---------------- consumers: warp `row` owns residual row `row` of the strip ------
+  // Software pipeline: iteration it runs phase A of strip it (X_L, rounded, into
+  // the staged tile; partial sums pushed to the cluster) and phase B of strip
+  // it - kLook (totals, rstd, m over the tile, TMA store), so the exchange of a
+  // strip overlaps the next strips' arithmetic.
+  constexpr int kLook = MatFinalPipe<T, LT>::kLook;
+  constexpr int kLag = MatFinalPipe<T, LT>::kStoreLag;
+  constexpr int kXS = MatFinalPipe<T, LT>::kXSlots;
+  constexpr int kRing = MatFinalPipe<T, LT>::kRing;
+  static_assert(kRing >= kLook + kLag + 2, "an output tile is rewritten only after its store has read it");
   const int row = warp;
   const int64_t c = c0 + 2 * lane;
   const bool cvalid = c < p.C;
@@ -260,71 +272,70 @@ __global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
   constexpr uint32_t kEs = sizeof(T);
   const bool storer = warp == 0 && lane == 0;
   const int grp = lane >> 3;  // 16-byte chunk (4 tokens) this lane sends
-  int done = 0;               // strips whose partials this warp has consumed and released
-  StripCursor cur(s_begin, p.G, p.strips_per_row);
+  int sent = 0;               // strips whose partials this warp has pushed to the cluster
+  bool ok = true;             // this warp's waits so far succeeded
+  StripCursor curB(s_begin, p.G, p.strips_per_row);
 
-  // A failed (timed-out) wait in any consumer warp ends the loop for all of them
-  // together: the strip's consumer barrier also ANDs the warps' status.
-  for (int it = 0; it < n_it; ++it, cur.next()) {
-    const int s = it % Lay::kStages;
-    const int x = it % kMatFinalXSlots;
-    if (storer) mbar_arrive_expect_tx(&xfull[x], static_cast<uint32_t>(nsl * kStripTokens * 4));
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / Lay::kStages) & 1));
-    if (ok && cur.b != mod_b) {  // the image's modulation rows (a strip lies in one image)
-      mod_b = cur.b;
-      if (cvalid) {
-        const T* shp = static_cast<const T*>(q.shift) + mod_b * q.mod_stride;
-        const T* scp = static_cast<const T*>(q.scale) + mod_b * q.mod_stride;
-        shv = make_float2(act_load(shp, c), act_load(shp, c + 1));
-        s1r = P2::rn(make_float2(__fadd_rn(1.f, act_load(scp, c)), __fadd_rn(1.f, act_load(scp, c + 1))));
-      }
-    }
-    const uint32_t sb = smem_base + s * Lay::kStageBytes;
-
-    // X_L of the warp's 16 tokens (cell k, column col), rounded like the
-    // materialisation's output, and each token's partial sum of squares.
-    float2 xr[16];
-    float sq[16];
-    if (ok) {
+  for (int it = 0; it < n_it + kLook; ++it) {
+    // ---------------- phase A: strip it ----------------------------------------
+    if (it < n_it && ok) {
+      const int s = it % Lay::kStages;
+      const int x = it % kXS;
+      if (storer) mbar_arrive_expect_tx(&xfull[x], static_cast<uint32_t>(nsl * kStripTokens * 4));
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (it / Lay::kStages) & 1));
+      if (ok) {
+        const uint32_t sb = smem_base + s * Lay::kStageBytes;
+        const uint32_t ob = smem_base + Lay::kRingOffset + (it % kRing) * Lay::kTileBytes;
+        float sq[16];
 #pragma unroll
-      for (int k = 0; k < kStripCells; ++k) {
-        const uint32_t xa = sb + ((row * kBoxCols + 4 * k) * kSliceCh + 2 * lane) * kEs;
-        float2 acc[4];
+        for (int k = 0; k < kStripCells; ++k) {
+          const uint32_t tok = ((row * kBoxCols + 4 * k) * kSliceCh + 2 * lane) * kEs;
+          const uint32_t xa = sb + tok;
+          float2 acc[4];
 #pragma unroll
-        for (int col = 0; col < 4; ++col) acc[col] = lds_pair<T>(xa + col * kSliceCh * kEs);
+          for (int col = 0; col < 4; ++col) acc[col] = lds_pair<T>(xa + col * kSliceCh * kEs);
 #pragma unroll
-        for (int l = 0; l < LMAX; ++l) {
-          if (l < L) {
-            const float2 d =
-                lds_pair<T>(sb + Lay::Base::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
+          for (int l = 0; l < LMAX; ++l) {
+            if (l < L) {
+              const float2 d =
+                  lds_pair<T>(sb + Lay::Base::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
-            for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
+              for (int col = 0; col < 4; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
+            }
+          }
+#pragma unroll
+          for (int col = 0; col < 4; ++col) {
+            const R rr = P2::rn(acc[col]);  // X_L as the materialisation stores it
+            sts_raw<T>(ob + tok + col * kSliceCh * kEs, rr);
+            const float2 v = P2::f(rr);
+            sq[4 * k + col] = __fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y));
           }
         }
-#pragma unroll
-        for (int col = 0; col < 4; ++col) {
-          const float2 v = P2::f(P2::rn(acc[col]));
-          xr[4 * k + col] = v;
-          sq[4 * k + col] = __fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // the load stage is free for the next strips
+        const float part = reduce_scatter16(sq, lane);  // lanes 2t, 2t + 1: token t of this row
+        float4 chunk;
+        chunk.x = __shfl_sync(0xffffffffu, part, 8 * grp + 0);
+        chunk.y = __shfl_sync(0xffffffffu, part, 8 * grp + 2);
+        chunk.z = __shfl_sync(0xffffffffu, part, 8 * grp + 4);
+        chunk.w = __shfl_sync(0xffffffffu, part, 8 * grp + 6);
+        // The slot's previous strip must be released by every receiver.
+        if (it >= kXS) ok = __all_sync(0xffffffffu, mbar_wait(&xempty[x], ((it / kXS) - 1) & 1));
+        if (ok) {
+          const uint32_t off = ((x * kMatFinalMaxSlices + rank) * kStripTokens + row * 16 + 4 * grp) * 4;
+          const uint32_t bar = smem_u32(&xfull[x]);
+          for (int pr = lane & 7; pr < nsl; pr += 8)
+            st_async_v4(mapa_shared(recv_base + off, pr), chunk, mapa_shared(bar, pr));
+          sent = it + 1;
         }
       }
-      const float part = reduce_scatter16(sq, lane);  // lanes 2t, 2t + 1: token t of this row
-      float4 chunk;
-      chunk.x = __shfl_sync(0xffffffffu, part, 8 * grp + 0);
-      chunk.y = __shfl_sync(0xffffffffu, part, 8 * grp + 2);
-      chunk.z = __shfl_sync(0xffffffffu, part, 8 * grp + 4);
-      chunk.w = __shfl_sync(0xffffffffu, part, 8 * grp + 6);
-      // The slot's previous strip must be released by every receiver.
-      if (it >= kMatFinalXSlots)
-        ok = __all_sync(0xffffffffu, mbar_wait_cluster(&xempty[x], ((it / kMatFinalXSlots) - 1) & 1));
-      if (ok) {
-        const uint32_t off = ((x * kMatFinalMaxSlices + rank) * kStripTokens + row * 16 + 4 * grp) * 4;
-        const uint32_t bar = smem_u32(&xfull[x]);
-        for (int pr = lane & 7; pr < nsl; pr += 8)
-          st_async_v4(mapa_shared(recv_base + off, pr), chunk, mapa_shared(bar, pr));
-        ok = __all_sync(0xffffffffu, mbar_wait_cluster(&xfull[x], (it / kMatFinalXSlots) & 1));
-      }
     }
+    // ---------------- phase B: strip j = it - kLook ------------------------------
+    const int j = it - kLook;
+    if (j < 0) continue;
+    const int x = j % kXS;
+    const uint32_t sb = smem_base + Lay::kRingOffset + (j % kRing) * Lay::kTileBytes;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&xfull[x], (j / kXS) & 1));
     if (ok) {
       // Token totals in slice order (identical in every CTA of the cluster), rstd.
       float r = 0.f;
@@ -334,35 +345,47 @@ __global__ void __launch_bounds__(BcastShape<LT, true>::kThreads, 2)
         for (int k = 0; k < nsl; ++k) tot = __fadd_rn(tot, rv[k * kStripTokens]);
         r = rsqrtf(__fadd_rn(__fmul_rn(tot, q.inv_c), q.eps));
       }
-      __syncwarp();
-      if (lane < nsl) mbar_remote_arrive(mapa_shared(smem_u32(&xempty[x]), lane));
-      done = it + 1;
-      // m = modulate(norm(X_L)) over the staged tile (the base tile's place).
+      if (curB.b != mod_b) {  // the image's modulation rows (a strip lies in one image)
+        mod_b = curB.b;
+        if (cvalid) {
+          const T* shp = static_cast<const T*>(q.shift) + mod_b * q.mod_stride;
+          const T* scp = static_cast<const T*>(q.scale) + mod_b * q.mod_stride;
+          shv = make_float2(act_load(shp, c), act_load(shp, c + 1));
+          s1r = P2::rn(make_float2(__fadd_rn(1.f, act_load(scp, c)), __fadd_rn(1.f, act_load(scp, c + 1))));
+        }
+      }
+      // m = modulate(norm(X_L)) over the staged tile.
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float rt = __shfl_sync(0xffffffffu, r, t);
-        const float2 tt = fmul2(xr[t], make_float2(rt, rt));
+        const uint32_t a = sb + ((row * kBoxCols + t) * kSliceCh + 2 * lane) * kEs;
+        const float2 tt = fmul2(lds_pair<T>(a), make_float2(rt, rt));
         const R nr = P2::rn(fmul2(tt, nw));
-        const R mv = P2::rn(fadd2(P2::f(P2::mul(nr, s1r)), shv));
-        sts_raw<T>(sb + ((row * kBoxCols + t) * kSliceCh + 2 * lane) * kEs, mv);
+        sts_raw<T>(a, P2::rn(fadd2(P2::f(P2::mul(nr, s1r)), shv)));
       }
       fence_proxy_async_smem();
     }
+    // A failed wait in any consumer warp ends the loop for all of them together.
     if (!named_barrier_and(1, 32 * Shape::kConsumerWarps, ok)) break;
+    // Every consumer warp has read slot x: release it to every sender (once per CTA).
+    if (warp == 0 && lane < nsl) mbar_remote_arrive(mapa_shared(smem_u32(&xempty[x]), lane));
     if (storer) {
-      tma_store_4d(&p.tm_out, smem + s * Lay::kStageBytes, static_cast<int32_t>(c0), 4 * cur.wx0(), 4 * cur.wy,
-                   static_cast<int32_t>(cur.b));
+      tma_store_4d(&p.tm_out, smem + Lay::kRingOffset + (j % kRing) * Lay::kTileBytes, static_cast<int32_t>(c0),
+                   4 * curB.wx0(), 4 * curB.wy, static_cast<int32_t>(curB.b));
       bulk_commit();
-      bulk_wait_read<Shape::kStoreLag>();
-      if (it >= Shape::kStoreLag) mbar_arrive(&empty[(it - Shape::kStoreLag) % Lay::kStages]);
+      // Before the next consumer barrier: at most kLag stores still read their tiles,
+      // so phase A may overwrite the tile of strip (next) - kRing.
+      bulk_wait_read<kLag>();
     }
+    curB.next();
   }
   if (storer) {
     bulk_wait_all();
-    // Do not leave while peers may still arrive on this CTA's slot barriers: wait
-    // for the releases of the last slots this CTA handed out.
-    for (int j = max(0, done - kMatFinalXSlots); j < done; ++j)
-      if (!mbar_wait_cluster(&xempty[j % kMatFinalXSlots], (j / kMatFinalXSlots) & 1)) break;
+    // Do not leave while peers may still arrive on this CTA's slot barriers: the
+    // receivers release each strip this CTA sent to every sender, so wait for the
+    // releases of the last strips sent.
+    for (int k = max(0, sent - kXS); k < sent; ++k)
+      if (!mbar_wait(&xempty[k % kXS], (k / kXS) & 1)) break;
   }
 }
 

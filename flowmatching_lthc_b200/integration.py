@@ -18,8 +18,8 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
   SharedReadLocalTHCSharedAdaLNJiT.forward_lazy (patch embedding + shared read
       fused on the tensor cores under bf16 autocast; each block's branch
-      epilogue, :318-323, fused with its lazy update; without autograd the
-      materialisation and the final layer's norm + modulate as one kernel)      :1374-1388
+      epilogue, :318-323, fused with its lazy update; with FUSE_FINAL and no
+      autograd, the materialisation and the final norm + modulate as one kernel) :1374-1388
 
 Shape checks and messages are the reference's own; the arithmetic runs in
 ``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
@@ -171,9 +171,11 @@ def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> to
     return self.unpatchify(self.final_layer(x_hi.reshape(b, hh * wh, c_dim), t2))
 
 
-# The inference forward fuses the materialisation with the final norm + modulate;
-# False keeps the two calls (tests compare the two forms).
-FUSE_FINAL = True
+# True: the inference forward runs the materialisation fused with the final norm +
+# modulate (lthc_materialise_final_fwd) instead of the two calls.  Off by default:
+# on B200 the fused kernel (0.51 ms at B = 64) is slower than the two kernels it
+# replaces (0.20 + 0.17 ms); its outputs equal theirs.
+FUSE_FINAL = False
 
 
 def _accumulate_betas(model, x0: torch.Tensor, updates: list[torch.Tensor]) -> list[torch.Tensor] | None:

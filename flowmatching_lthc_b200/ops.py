@@ -848,8 +848,14 @@ def materialise_final_supported(x0: Tensor, n_layers: int) -> bool:
         flag = ctypes.c_int(0)
         with _guard(x0):
             _lib.call("lthc_materialise_final_supported", c, n_layers, _DTYPE_CODE[x0.dtype], ctypes.byref(flag))
-        _MATFINAL_SUPPORT[key] = bool(flag.value)
-    return _MATFINAL_SUPPORT[key]
+        _MATFINAL_SUPPORT[key] = int(flag.value)
+    return _MATFINAL_SUPPORT[key] > 0
+
+
+def materialise_final_clusters(x0: Tensor, n_layers: int) -> int:
+    """How many clusters of the fused kernel the device holds at once (0: none)."""
+    return _MATFINAL_SUPPORT[(x0.device.index, x0.shape[-1], n_layers, x0.dtype)] if materialise_final_supported(
+        x0, n_layers) else 0
 
 
 @_custom_op("materialise_final")

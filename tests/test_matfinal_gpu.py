@@ -108,7 +108,7 @@ def _small_model(L):
 
 
 @pytest.mark.parametrize("released", [False, True])
-def test_model_inference_fused_equals_unfused(released):
+def test_model_inference_fused_equals_unfused(released, monkeypatch):
     """The installed inference forward with the fused final step against the same
     forward with the two calls (and, for the released B/4 model under bf16
     autocast, against the reference's own eager + Triton forward)."""
@@ -126,15 +126,21 @@ def test_model_inference_fused_equals_unfused(released):
         m = _small_model(L)
         x, t, y = inputs(2, 64, seed=4)
         ctx, tol = torch.autocast("cuda", enabled=False), 1e-5
+    calls = []
+    fused_op = ops.materialise_final
+    monkeypatch.setattr(ops, "materialise_final", lambda *a: calls.append(1) or fused_op(*a))
+    saved = integration.FUSE_FINAL
     with torch.no_grad(), ctx:
         ref = m(x, t, y)
         with integration.install(L):
-            fused = m(x, t, y)
-            integration.FUSE_FINAL = False
             try:
+                integration.FUSE_FINAL = True
+                fused = m(x, t, y)
+                integration.FUSE_FINAL = False
                 unfused = m(x, t, y)
             finally:
-                integration.FUSE_FINAL = True
+                integration.FUSE_FINAL = saved
+    assert len(calls) == 1  # the fused kernel ran for the FUSE_FINAL forward only
     assert ref.abs().max() > 0
     assert rel_err(fused, unfused) < tol
     assert rel_err(fused, ref) < tol
