@@ -137,7 +137,10 @@ int64_t slices_of(int64_t C) { return ceil_div(C, kSliceCh); }
 // Weight-gradient partials: one [L][C][16] fp32 block per CTA column of the read
 // kernel, whose grid is fixed at two CTAs per SM so that the workspace size is a
 // pure function of the shape and the SM count.
-constexpr int kWgradCtasPerSm = 2;
+#ifndef LTHC_WGRAD_CTAS_PER_SM
+#define LTHC_WGRAD_CTAS_PER_SM 2
+#endif
+constexpr int kWgradCtasPerSm = LTHC_WGRAD_CTAS_PER_SM;
 
 int64_t strips_of(int64_t B, int64_t G) { return B * G * ceil_div(G, kStripCells); }
 
@@ -486,8 +489,8 @@ int launch_read_t(PoolTmaParams& p, float* grad_w, int sms, cudaStream_t s) {
 template <typename T, bool POOL, bool WGRAD>
 int launch_read_l(PoolTmaParams& p, float* grad_w, int sms, cudaStream_t s) {
   if (p.L == 1) return launch_read_t<T, 1, POOL, WGRAD, 1>(p, grad_w, sms, s);
-  if (p.L == 12) return launch_read_t<T, 12, POOL, WGRAD, 4>(p, grad_w, sms, s);
-  return launch_read_t<T, 0, POOL, WGRAD, 4>(p, grad_w, sms, s);
+  if (p.L == 12) return launch_read_t<T, 12, POOL, WGRAD, LTHC_POOL_CELLS_DEEP>(p, grad_w, sms, s);
+  return launch_read_t<T, 0, POOL, WGRAD, LTHC_POOL_CELLS_DEEP>(p, grad_w, sms, s);
 }
 
 template <typename T>

@@ -119,8 +119,18 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr) {
   return v;
 }
 
+// Resident CTAs per SM the register allocation is sized for.
+#ifndef LTHC_READ_MIN_BLOCKS
+#define LTHC_READ_MIN_BLOCKS 2
+#endif
+// Cells per pooling warp for deep (L > 1) stacks.
+#ifndef LTHC_POOL_CELLS_DEEP
+#define LTHC_POOL_CELLS_DEEP 4
+#endif
+
 template <typename T, int LT, bool POOL, bool WGRAD, int CELLS_PER_POOL>
-__global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL, WGRAD, CELLS_PER_POOL>::kThreads, 2)
+__global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL, WGRAD, CELLS_PER_POOL>::kThreads,
+                                  LTHC_READ_MIN_BLOCKS)
     pool_tma_kernel(const __grid_constant__ PoolTmaParams p) {
   constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
   using Lay = PoolLayout<T, LMAX, POOL, WGRAD, CELLS_PER_POOL>;
