@@ -1291,7 +1291,9 @@ int lthc_final_norm_modulate_fwd(const void* x, const void* norm_weight, int w_d
   const bool nonempty = B > 0 && T > 0;
   LTHC_TRY(check_act(x, "x", nonempty));
   LTHC_TRY(check_act(out, "out", nonempty));
-  if (!norm_weight || !shift || !scale) return fail(LTHC_ERR_NULL_POINTER, "norm_weight, shift and scale must be set");
+  // shift / scale are [B, C]: NULL is valid for an empty batch only
+  if (!norm_weight || (B > 0 && (!shift || !scale)))
+    return fail(LTHC_ERR_NULL_POINTER, "norm_weight, shift and scale must be set");
   if (!nonempty) return LTHC_OK;
   int sms = 0;
   LTHC_TRY(current_device(&sms));
@@ -1315,7 +1317,7 @@ int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight, int w_d
   LTHC_TRY(check_act(x, "x", nonempty));
   LTHC_TRY(check_act(grad_out, "grad_out", nonempty));
   LTHC_TRY(check_act(grad_x, "grad_x", nonempty));
-  if (!norm_weight || !scale) return fail(LTHC_ERR_NULL_POINTER, "norm_weight and scale must be set");
+  if (!norm_weight || (B > 0 && !scale)) return fail(LTHC_ERR_NULL_POINTER, "norm_weight and scale must be set");
   if (!nonempty && !grad_weight && (B == 0 || (!grad_shift && !grad_scale))) return LTHC_OK;
   int sms = 0;
   LTHC_TRY(current_device(&sms));
@@ -1363,7 +1365,7 @@ int lthc_materialise_final_fwd(const void* x0, const void* const* dz, const void
   LTHC_TRY(check_act(x0, "x0", B > 0));
   LTHC_TRY(check_act(m_out, "m_out", B > 0));
   LTHC_TRY(check_ptr(norm_weight, "norm_weight"));
-  if (!shift || !scale) return fail(LTHC_ERR_NULL_POINTER, "shift / scale is NULL");
+  if (B > 0 && (!shift || !scale)) return fail(LTHC_ERR_NULL_POINTER, "shift / scale is NULL");
   for (int l = 0; l < n_layers; ++l) {
     LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
     LTHC_TRY(check_ptr(beta[l], "beta[l]"));

@@ -147,3 +147,21 @@ def test_validation():
     with pytest.raises(ValueError):
         ops.branch_lazy_update(d["z"][..., :60], d["attn"][..., :60], d["mlp"][..., :60], d["gate"][:, :60],
                                d["alpha"][:60], d["beta"][:60])  # C not a multiple of 8
+
+
+def test_unaligned_gate_view_and_empty_batch():
+    """A gate view whose rows are not 16-byte aligned is copied before the call;
+    an empty batch returns empty outputs and zero weight gradients."""
+    _, d = make(2, 32, 64, torch.bfloat16, seed=9)
+    t = torch.randn(2, 6 * 64 + 1, device="cuda").to(torch.bfloat16)
+    gate = t[:, 1:65]  # starts 2 bytes into the row
+    assert gate.data_ptr() % 16 != 0
+    a = ops.branch_lazy_update(d["z"], d["attn"], d["mlp"], gate, d["alpha"], d["beta"])
+    b = ops.branch_lazy_update(d["z"], d["attn"], d["mlp"], gate.contiguous(), d["alpha"], d["beta"])
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    e = torch.empty(0, 16, 64, device="cuda", dtype=torch.bfloat16)
+    ge = torch.empty(0, 64, device="cuda", dtype=torch.bfloat16)
+    dz, zn = ops.branch_lazy_update(e, e, e, ge, d["alpha"], d["beta"])
+    assert dz.shape == e.shape and zn.shape == e.shape
+    g_attn, g_mlp, g_gate, ga, gb = ops.branch_lazy_update_bwd(None, e, e, e, ge, d["alpha"], d["beta"])
+    assert g_gate.shape == (0, 64) and torch.count_nonzero(ga) == 0 and torch.count_nonzero(gb) == 0

@@ -139,6 +139,10 @@ def test_empty_and_validation():
     assert ops.final_norm_modulate(x, w, shift, scale, 1e-6).shape == (2, 0, 768)
     gx, gw, gsh, gsc = ops.final_norm_modulate_bwd(gm, x, w, scale, 1e-6)
     assert gx.shape == (2, 0, 768) and not gw.any() and not gsh.any() and not gsc.any()
+    x, w, shift, scale, gm = inputs(0, 16, 768, torch.bfloat16, seed=1)  # empty batch: [0, C] modulation rows
+    assert ops.final_norm_modulate(x, w, shift, scale, 1e-6).shape == (0, 16, 768)
+    gx, gw, gsh, gsc = ops.final_norm_modulate_bwd(gm, x, w, scale, 1e-6)
+    assert gx.shape == (0, 16, 768) and gsh.shape == (0, 768) and not gw.any()
     x, w, shift, scale, _ = inputs(2, 8, 768, torch.bfloat16, seed=1)
     with pytest.raises(ValueError):
         ops.final_norm_modulate(x, w, shift.float(), scale.float(), 1e-6)  # dtype mix

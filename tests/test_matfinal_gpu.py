@@ -144,3 +144,17 @@ def test_model_inference_fused_equals_unfused(released, monkeypatch):
     assert ref.abs().max() > 0
     assert rel_err(fused, unfused) < tol
     assert rel_err(fused, ref) < tol
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_empty_batch_and_smallest_channel_count(dtype):
+    x0, dz, betas, nw, t2 = make(0, 4, 64, 2, dtype, seed=5)
+    cu = lambda t: t.cuda()  # noqa: E731
+    shift, scale = cu(t2).chunk(2, dim=1)
+    m = ops.materialise_final(cu(x0), [cu(t) for t in dz], [cu(t) for t in betas], cu(nw), shift, scale, 1e-6)
+    assert m.shape == x0.shape
+    x0, dz, betas, nw, t2 = make(3, 4, 8, 2, dtype, seed=6)  # C = 8: one slice, 4 valid lanes
+    t2c = cu(t2)
+    m = ops.materialise_final(cu(x0), [cu(t) for t in dz], [cu(t) for t in betas], cu(nw), t2c[:, :8], t2c[:, 8:],
+                              1e-6)
+    check(m, two_kernel(cu(x0), [cu(t) for t in dz], [cu(t) for t in betas], cu(nw), t2c[:, :8], t2c[:, 8:]), dtype)
