@@ -6,6 +6,7 @@ parity suite.
 """
 from __future__ import annotations
 
+import functools
 import os
 import sys
 from pathlib import Path
@@ -24,6 +25,7 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: full-size (benchmark-configuration) cases")
 
 
+@functools.lru_cache(maxsize=1)
 def _cuda_ok() -> bool:
     try:
         import torch
@@ -39,6 +41,27 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _device_error_word(request):
+    """After every GPU test: the library's device error word must be clear.  A
+    kernel whose bounded wait gave up sets it and returns without finishing its
+    work, so a test that passed with the word set would hide a timeout."""
+    yield
+    if "gpu" not in request.keywords or not _cuda_ok():
+        return
+    import ctypes
+
+    import torch
+
+    from flowmatching_lthc_b200 import _lib
+
+    if _lib._lib is None:  # the test never loaded the library
+        return
+    st = ctypes.c_int(-1)
+    _lib.call("lthc_device_status", ctypes.byref(st), torch.cuda.current_stream().cuda_stream)
+    assert st.value == 0, "a bounded device-side wait gave up during this test (LTHC_ERR_TIMEOUT)"
 
 
 def reference_available() -> bool:
