@@ -117,6 +117,11 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
   __syncthreads();
   tmem_fence_after_sync();
   const uint32_t tmem = *tslot;
+  // Z pooling: this thread's channel pair and its 16 read weights (fixed for the kernel)
+  const int zn = 2 * (tid % (kEmbedChunk / 2));
+  float2 za[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) za[r] = *reinterpret_cast<const float2*>(alpha_s + r * kEmbedChunk + zn);
   const uint32_t tmem_d1 = tmem;
   const uint32_t tmem_d2 = tmem + kEmbedBottleneck;
   const uint32_t idesc1 = umma_idesc_bf16_f32(kEmbedTileTokens, kEmbedBottleneck);
@@ -255,8 +260,8 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 conv = bf16_round2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
-            const __nv_bfloat162 t =
-                __floats2bfloat162_rn(__fadd_rn(conv.x, bias_s[n + 2 * e]), __fadd_rn(conv.y, bias_s[n + 2 * e + 1]));
+            const float2 bb = *reinterpret_cast<const float2*>(bias_s + n + 2 * e);
+            const __nv_bfloat162 t = __floats2bfloat162_rn(__fadd_rn(conv.x, bb.x), __fadd_rn(conv.y, bb.y));
             o[e] = *reinterpret_cast<const uint32_t*>(&t);
           }
           uint4 w;
@@ -285,19 +290,18 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
     // ---- Z: pool the staged X0 over each cell's 16 positions (r = 0..15 in order, fp32 FMA)
     const int64_t zrow0 = b * static_cast<int64_t>(cell_rows) * (p.H / 4) + static_cast<int64_t>(wy) * (p.H / 4) +
                           (kEmbedTileCols / 4) * hx;
+    static_assert(kEmbedThreads % (kEmbedChunk / 2) == 0, "each thread pools one fixed channel pair");
     for (int pi = tid; pi < 8 * (kEmbedChunk / 2); pi += kEmbedThreads) {
       const int cell = pi / (kEmbedChunk / 2);
-      const int n = 2 * (pi % (kEmbedChunk / 2));
       float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
         const int R = (r >> 2) * kEmbedTileCols + 4 * cell + (r & 3);
-        const uint32_t raw =
-            *reinterpret_cast<const uint32_t*>(smem + EmbedSmem::kX + (n >> 6) * 16384 + sw128_offset(R, n & 63));
-        const float2 a = *reinterpret_cast<const float2*>(alpha_s + r * kEmbedChunk + n);
-        acc = ffma2(a, Act<__nv_bfloat16>::cvt(raw), acc);
+        const uint32_t raw = *reinterpret_cast<const uint32_t*>(smem + EmbedSmem::kX + (zn >> 6) * 16384 +
+                                                                sw128_offset(R, zn & 63));
+        acc = ffma2(za[r], Act<__nv_bfloat16>::cvt(raw), acc);
       }
-      Act<__nv_bfloat16>::st(p.z + (zrow0 + cell) * p.C + n0 + n, acc);
+      Act<__nv_bfloat16>::st(p.z + (zrow0 + cell) * p.C + n0 + zn, acc);
     }
   }
   if (tid == 0) bulk_wait_all();
