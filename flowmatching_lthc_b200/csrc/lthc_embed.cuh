@@ -181,20 +181,10 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
       }
     }
   };
-  if (cta_in_chunk < p.tiles) gather_load(cta_in_chunk);
-
-  for (int64_t tile = cta_in_chunk; alive && tile < p.tiles; tile += ctas_per_chunk, ++it) {
-    const int64_t b = tile / (cell_rows * halves);
-    const int rem = static_cast<int>(tile - b * cell_rows * halves);
-    const int wy = rem / halves, hx = rem % halves;
-
-    // ---- A1: the tile's patches (loaded into registers during the previous tile)
-    gather_store(pre);
-    fence_proxy_async_smem();
-    tmem_fence_before_sync();
-    __syncthreads();
-
-    // ---- GEMM 1
+  // Tile pipeline: the next tile's patches are staged while this tile's GEMM 2
+  // runs, and its GEMM 1 is issued before this tile's Z pooling, so both overlap
+  // work of the current tile.
+  auto issue_gemm1 = [&]() {
     if (tid == 0) {
       tmem_fence_after_sync();
       for (int s = 0; s < p.in_ch; ++s)
@@ -202,7 +192,24 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
                   umma_desc_sw128(sbase + EmbedSmem::kW1 + 32 * s), idesc1, s > 0);
       umma_commit(bar1);
     }
-    if (tile + ctas_per_chunk < p.tiles) gather_load(tile + ctas_per_chunk);  // overlaps the rest of this tile
+  };
+  if (cta_in_chunk < p.tiles) {
+    gather_load(cta_in_chunk);
+    gather_store(pre);
+    fence_proxy_async_smem();
+    tmem_fence_before_sync();
+    __syncthreads();
+    issue_gemm1();
+    if (cta_in_chunk + ctas_per_chunk < p.tiles) gather_load(cta_in_chunk + ctas_per_chunk);
+  }
+
+  for (int64_t tile = cta_in_chunk; alive && tile < p.tiles; tile += ctas_per_chunk, ++it) {
+    const int64_t b = tile / (cell_rows * halves);
+    const int rem = static_cast<int>(tile - b * cell_rows * halves);
+    const int wy = rem / halves, hx = rem % halves;
+    const bool has_next = tile + ctas_per_chunk < p.tiles;
+
+    // ---- GEMM 1 of this tile (issued before the previous tile's Z pooling)
     bool ok = mbar_wait(bar1, it & 1);
     tmem_fence_after_sync();
 
@@ -241,6 +248,8 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
                   umma_desc_sw128(sbase + EmbedSmem::kW2 + (s >> 2) * 32768 + 32 * (s & 3)), idesc2, s > 0);
       umma_commit(bar2);
     }
+    // the next tile's patches into A1 (GEMM 1 of this tile has completed) while GEMM 2 runs
+    if (has_next) gather_store(pre);
     ok = mbar_wait(bar2, it & 1);
     tmem_fence_after_sync();
 
@@ -277,6 +286,10 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
     tmem_fence_before_sync();
     alive = __syncthreads_and(ok);
     if (!alive) break;
+
+    // ---- GEMM 1 of the next tile (its patches are staged, D1 was read by epilogue 1)
+    if (has_next) issue_gemm1();
+    if (tile + 2 * ctas_per_chunk < p.tiles) gather_load(tile + 2 * ctas_per_chunk);
 
     // ---- X0 out: four TMA tile stores of 64 channels x 32 columns x 4 rows
     if (tid == 0) {
