@@ -512,12 +512,16 @@ def main() -> int:
 
     cfg = _op_inputs(B, dev, seed=1000 + r.rank)
     step, bytes_step, launches, kernel = op_step(args.op, cfg)
-    for _ in range(max(args.warmup, 3)):
-        step()
+    step()
     torch.cuda.synchronize()
 
+    # The clock sampler starts first; the warm-up steps then run directly before
+    # the timed region, so the GPU enters it busy rather than after an idle gap
+    # (an idle GPU lowers its clocks, which a timed region of a few ms would see).
     sampler = ClockSampler() if r.is_main else None
     time.sleep(0.3 if sampler else 0)
+    for _ in range(max(args.warmup, 3)):
+        step()
     D.barrier()
     torch.cuda.synchronize()
     t_wall0 = time.time()

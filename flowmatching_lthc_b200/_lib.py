@@ -1,7 +1,7 @@
 """ctypes binding of the C ABI in ``include/lthc_b200.h``.
 
 This is the same stub a Python user of the reference would add to call the
-library (see INTEGRATION.md).  Loading fails loudly: there is no CPU fallback.
+library.  Loading fails loudly: there is no CPU fallback.
 """
 from __future__ import annotations
 

@@ -64,16 +64,26 @@ def _device_error_word(request):
     assert st.value == 0, "a bounded device-side wait gave up during this test (LTHC_ERR_TIMEOUT)"
 
 
+def reference_root() -> Path | None:
+    """Where the reference package (tongtongliang/flowmatching_lthc) can be
+    imported from: an explicit checkout named by LTHC_REFERENCE, else the copy
+    installed under baseline/_ref.  None when neither exists."""
+    for cand in (os.environ.get("LTHC_REFERENCE"), REF):
+        if cand and (Path(cand) / "flowmatching_lthc" / "__init__.py").exists():
+            return Path(cand)
+    return None
+
+
 def reference_available() -> bool:
-    """The reference package (tongtongliang/flowmatching_lthc) installed under baseline/_ref."""
-    return (REF / "flowmatching_lthc" / "__init__.py").exists()
+    return reference_root() is not None
 
 
 def import_reference():
-    if not reference_available():
-        pytest.skip("reference package not installed under baseline/_ref")
-    if str(REF) not in sys.path:
-        sys.path.insert(0, str(REF))
-    os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
+    root = reference_root()
+    if root is None:
+        pytest.skip("reference package not importable (set LTHC_REFERENCE or install it under baseline/_ref)")
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    sys.dont_write_bytecode = True  # the reference checkout may be read-only
     import flowmatching_lthc.models.local_thc as L  # noqa: F401
     return L

@@ -35,7 +35,10 @@ from pathlib import Path
 import torch
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("LTHC_REFERENCE", "/root/reference"))
+if not os.environ.get("LTHC_REFERENCE"):
+    sys.exit("set LTHC_REFERENCE to the root of a flowmatching_lthc checkout (the directory that holds "
+             "flowmatching_lthc/models/local_thc.py)")
+sys.path.insert(0, os.environ["LTHC_REFERENCE"])
 sys.dont_write_bytecode = True
 
 from flowmatching_lthc.models import local_thc as L  # noqa: E402

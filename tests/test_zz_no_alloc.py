@@ -5,10 +5,13 @@ synchronise the device).  It keeps its partial sums in a fixed buffer inside the
 library instead of a caller workspace.
 
 The test calls it through the C ABI twice in a row, on different inputs (so a
-second call that reused stale contents of the shared buffer would be caught),
-and compares each result with lthc_weight_grad given a normal workspace, at the
-tolerance the other weight-gradient tests use.  It also checks that a shape
-whose partial sums do not fit the buffer is refused before anything runs.
+second call that reused stale contents of the shared buffer would be caught).
+Both entry points run the same kernels in the same fixed reduction order and
+differ only in where the partial sums live, so each result must equal
+lthc_weight_grad's (given a normal workspace) bit for bit; it is also checked
+against the CPU oracle's weight gradient at the tolerance the other
+weight-gradient tests use (the oracle sums in another order).  A shape whose
+partial sums do not fit the buffer must be refused before anything runs.
 This file is collected last so that a failure here stops a -x run only after
 every other test has run; it needs nothing from the other test files.
 """
@@ -18,6 +21,7 @@ import pytest
 import torch
 
 from flowmatching_lthc_b200 import _lib
+from oracle import lthc_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -64,7 +68,9 @@ def test_noalloc_weight_grad_matches_the_workspace_entry_point_on_two_calls(B, G
         got = without_workspace(high, low, B, G, C)
         torch.cuda.synchronize()
         assert torch.isfinite(got).all(), f"call {call}: output not fully written"
-        assert rel_err(got, ref) < RTOL_REDUCTION, f"call {call}"
+        assert torch.equal(got, ref), f"call {call}: differs from lthc_weight_grad"
+        want = O.weight_grad(high.cpu(), [t.cpu() for t in low])
+        assert rel_err(got, want) < RTOL_REDUCTION, f"call {call}: differs from the oracle"
 
 
 def test_noalloc_refuses_shapes_beyond_its_buffer():
