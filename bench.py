@@ -53,8 +53,12 @@ def parse_args():
     p.add_argument("--batch", type=int, default=B_DEFAULT, help="images per GPU (BASELINE config 2: 64)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     p.add_argument("--no-extras", action="store_true", help="skip the per-kernel and comparator measurements")
-    p.add_argument("--op", default="materialise_fwd", choices=sorted(OPS + MODEL_OPS),
+    p.add_argument("--op", default="materialise_fwd", choices=sorted(OPS),
                    help="the LTHC op timed as the step (default: the BASELINE config 2 materialisation)")
+    p.add_argument("--no-model", action="store_true",
+                   help="skip the LTHC-B/4 images/sec legs (forward, training step, sampling)")
+    p.add_argument("--reference-gpu", action="store_true",
+                   help="also time the reference's own model on the GPU (needs the reference package)")
     return p.parse_args()
 
 
@@ -142,6 +146,27 @@ def time_device(fn, iters: int, stream: torch.cuda.Stream) -> float:
     return start.elapsed_time(end) / iters
 
 
+def host_link(h_src: torch.Tensor, d_buf: torch.Tensor, r: D.Rank, dev, stream) -> dict:
+    """Pinned host<->device copy bandwidth of this rank while every rank copies at
+    once (barrier-aligned): the ceiling of an end-to-end leg whose inputs and
+    results cross the host link.  GB/s per rank, slowest rank."""
+    n = min(h_src.numel(), d_buf.numel())
+    src, dst = h_src.reshape(-1)[:n], d_buf.reshape(-1)[:n]
+    nbytes = n * h_src.element_size()
+    out = {}
+    for name, fn in (("h2d", lambda: dst.copy_(src, non_blocking=True)),
+                     ("d2h", lambda: src.copy_(dst, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        D.barrier()
+        ms = D.reduce_max(time_device(fn, 3, stream), dev)
+        out[f"{name}_gbs"] = round(nbytes / (ms / 1e3) / 1e9, 2)
+    out["bytes_per_copy"] = nbytes
+    out["aggregate_h2d_gbs"] = round(out["h2d_gbs"] * r.world, 1)
+    out["aggregate_d2h_gbs"] = round(out["d2h_gbs"] * r.world, 1)
+    return out
+
+
 def host_threads() -> int:
     """All host threads this process may run on (torchrun sets OMP_NUM_THREADS=1,
     so the CPU legs set their thread count explicitly)."""
@@ -169,7 +194,46 @@ def cpu_baseline(seconds: float) -> dict:
             break
     by = W.materialise_bytes(Bs, G, C, L, 2) * n
     return {"value": round(by / el / 1e9, 4), "unit": UNIT, "cores": O.num_threads(), "kind": "port",
-            "sample": f"{n} x materialise of B={Bs} (config 2 shapes, bf16) in {el:.1f} s on {O.num_threads()} threads"}
+            "sample": f"{n} x materialise of B={Bs} (config 2 shapes, bf16) in {el:.1f} s on {O.num_threads()} threads",
+            "scope": "one process on every host thread: the whole host CPU, compared with all GPUs of the job"}
+
+
+def reference_eager_cpu(Bs: int, seconds: float) -> dict | None:
+    """The reference's own CPU path for the materialisation, timed when the reference
+    package is importable (LTHC_REFERENCE or baseline/_ref): its pure-torch loop of
+    12 write_add calls (local_thc.py:1368-1372, 1275-1276) in torch eager on every
+    host thread, bf16 as under autocast.  None when the package is absent."""
+    for cand in (os.environ.get("LTHC_REFERENCE"), str(ROOT / "baseline" / "_ref")):
+        if cand and (Path(cand) / "flowmatching_lthc").exists() and cand not in sys.path:
+            sys.path.insert(0, cand)
+    try:
+        sys.dont_write_bytecode = True
+        from flowmatching_lthc.models import local_thc as Lr
+    except Exception:
+        return None
+    torch.set_num_threads(host_threads())
+    cfg = W.config2(B=Bs, seed=0)
+    writes = []
+    for p in cfg["P"]:
+        w = Lr.LayerLocalWrite(4 * G, G, C, C)
+        with torch.no_grad():
+            w.write_weight.copy_(p)
+        writes.append(type("Blk", (), {"write": w})())
+    holder = type("M", (), {"blocks": writes})()
+    fn = Lr.SharedReadLocalTHCSharedAdaLNJiT.final_accumulate_reference
+    with torch.no_grad():
+        fn(holder, cfg["x0"], cfg["dz"])
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn(holder, cfg["x0"], cfg["dz"])
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+    by = W.materialise_bytes(Bs, G, C, L, 2) * n
+    return {"value": round(by / el / 1e9, 4), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"{n} x the reference's final_accumulate_reference (12 x write_add, torch eager) at B={Bs}, "
+                      f"bf16, in {el:.1f} s"}
 
 
 # ------------------------------------------------------------------ ops
@@ -250,140 +314,167 @@ def op_step(op: str, cfg: dict):
 
 OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
        "final_fwd", "final_bwd", "embed_fwd", "branch_fwd", "branch_bwd", "materialise_final_fwd")
-MODEL_OPS = ("model_fwd", "train_step", "sample")
-# Largest batch per model call for which the reference Triton materialisation's
-# 32-bit element offsets stay in range at 64x64x768 (2^31 / (4096 * 768)).
-REF_TRITON_MAX_BATCH = (2**31 - 1) // (4096 * 768)
 
 
 # ------------------------------------------------------------------ model-level workloads
-def _reference_model(dev):
-    """The released LTHC-B/4 model from the reference package (baseline/_ref), random
-    init with its zero-initialised layers (AdaLN, final linear) re-seeded so that the
-    output is not identically zero."""
-    ref = ROOT / "baseline" / "_ref"
-    if not (ref / "flowmatching_lthc").exists():
-        raise RuntimeError("model-level workloads need the reference package under baseline/_ref")
-    sys.path.insert(0, str(ref))
-    import flowmatching_lthc.models.local_thc as Lm
-    from flowmatching_lthc.models import build_model
-
-    torch.manual_seed(0)
-    m = build_model("lthc_b4_velocity").to(dev)
-    g = torch.Generator().manual_seed(1)
-    with torch.no_grad():
-        for name, prm in m.named_parameters():
-            if name.endswith("read_logits"):
-                prm.copy_(torch.randn(prm.shape, generator=g))
-            elif name.endswith("write_weight"):
-                prm.copy_(1.0 + 0.1 * torch.randn(prm.shape, generator=g))
-            elif torch.count_nonzero(prm) == 0:
-                prm.copy_(0.02 * torch.randn(prm.shape, generator=g))
-    return m, Lm
+SAMPLE_IMAGES = 1024       # Heun-50, CFG 1.5, 1024 images sharded over the GPUs
+SAMPLE_CHUNK = 512         # images per captured sampling graph (a doubled batch of 1024 per model call)
 
 
-def model_bench(args, r: D.Rank, dev, stream) -> dict:
-    """Images/sec of the reference model with the LTHC interface on the new kernels
-    (integration.install) and with the reference's own GPU path (eager + Triton),
-    same process, same inputs.  model_fwd = BASELINE config 3 (B=64 bf16 forward);
-    train_step = config 4 (32 images per GPU, fwd + bwd + fused AdamW, DDP for N>1);
-    sample = config 5 (Heun-50, CFG 1.5, 1024 images sharded over the GPUs; ours
-    uses the doubled-batch sampler, the reference its two-call sampler)."""
-    from flowmatching_lthc_b200 import integration
-    from flowmatching_lthc_b200.sampling import sample_heun as sample_doubled
+def _model(dev, seed: int = 1):
+    """LTHC-B/4 (flowmatching_lthc_b200.model) with seeded random weights (every layer
+    non-zero, so no work is trivially zero)."""
+    from flowmatching_lthc_b200.model import build_model, fill_seeded_
 
-    m, Lm = _reference_model(dev)
+    return fill_seeded_(build_model("lthc_b4_velocity"), seed).to(dev)
+
+
+def _timed(step, steps: int, stream) -> float:
+    """Device ms of `steps` calls of step(), max over ranks, barrier + sync on both sides."""
+    D.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    D.barrier()
+    return D.reduce_max(e0.elapsed_time(e1), stream.device)
+
+
+def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
+    """Images/sec of the LTHC-B/4 model at N GPUs (whole-job aggregates, device time,
+    max over ranks), bf16 autocast, seeded synthetic inputs:
+      forward   BASELINE config 3: B = 64 per GPU;
+      train     config 4: fwd + bwd + fused AdamW, 32 images per GPU, DDP (NCCL
+                all-reduce of every gradient) for N > 1;
+      sample    config 5: Heun-50 CFG 1.5 (velocity target) of 1024 images, host-seeded
+                per-image noise and labels sharded over the ranks, doubled batch,
+                each chunk of <= 512 images one captured CUDA graph.
+    With `reference_gpu` (needs the reference package importable), the reference's
+    own model with identical weights is timed on the same inputs: forward and train
+    step with its eager LTHC + Triton materialisation, sampling with its two-call
+    sampler on chunks of <= 256 images (its Triton op's 32-bit offsets wrap above
+    682 images per call)."""
+    from flowmatching_lthc_b200.sampling import GraphedHeunSampler, image_noise
+
+    out: dict = {}
     gen = torch.Generator(device=dev).manual_seed(2000 + r.rank)
-    op = args.op
-    if op == "model_fwd":
-        B = args.batch
-        m.eval()
-        x = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
-        t = torch.rand(B, device=dev, generator=gen)
-        y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
+    m = _model(dev)
+    refm = _reference_model(dev) if reference_gpu else None
 
-        def step():
+    # config 3: forward at B = 64 per GPU
+    B = 64
+    x = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+    t = torch.rand(B, device=dev, generator=gen)
+    y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
+    leg = {}
+    for tag, net in (("ours", m), ("reference", refm)):
+        if net is None:
+            continue
+        net.eval()
+
+        def fwd(net=net):
             with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
-                m(x, t, y)
-        per_step, warm, steps = B, max(args.warmup, 3), args.steps
-    elif op == "train_step":
-        B = 32
-        m.train()
-        net = m
-        if r.world > 1:
-            net = torch.nn.parallel.DistributedDataParallel(m, device_ids=[r.local_rank])
-        opt = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True)
-        x1 = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
-        x0 = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
-        t = torch.rand(B, device=dev, generator=gen)
-        y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
-        tt = t.view(-1, 1, 1, 1)
-        z = tt * x1 + (1 - tt) * x0
-        v = (x1 - z) / (1 - tt).clamp_min(0.05)
+                net(x, t, y)
+        for _ in range(3):
+            fwd()
+        ms = _timed(fwd, 10, stream)
+        leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_batch": round(ms / 10, 3)}
+    out["forward"] = {"config": "BASELINE config 3: B=64 per GPU, bf16 autocast", "batch_per_gpu": B,
+                      "steps": 10, **leg.pop("ours"), **({"reference_gpu": leg["reference"]} if leg else {})}
 
-        def step():
+    # config 4: training step, 32 images per GPU
+    B = 32
+    x1 = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+    e = torch.randn(B, 3, 256, 256, device=dev, generator=gen)
+    t = torch.rand(B, device=dev, generator=gen)
+    y = torch.randint(0, 1000, (B,), device=dev, generator=gen)
+    tt = t.view(-1, 1, 1, 1)
+    zt = tt * x1 + (1 - tt) * e
+    v = (x1 - zt) / (1 - tt).clamp_min(0.05)
+    leg = {}
+    for tag, net0 in (("ours", m), ("reference", refm)):
+        if net0 is None:
+            continue
+        net0.train()
+        net = torch.nn.parallel.DistributedDataParallel(net0, device_ids=[r.local_rank]) if r.world > 1 else net0
+        opt = torch.optim.AdamW(net0.parameters(), lr=1e-4, fused=True)
+
+        def train(net=net, opt=opt):
             opt.zero_grad(set_to_none=True)
             with torch.autocast("cuda", dtype=torch.bfloat16):
-                loss = (v - net(z, t, y)).float().square().mean()
+                loss = (v - net(zt, t, y)).float().square().mean()
             loss.backward()
             opt.step()
-        per_step, warm, steps = B, max(args.warmup, 3), args.steps
-    else:  # sample
-        n_img = D.shard(1024, r.rank, r.world)
-        nb = n_img[1] - n_img[0]
-        m.eval()
-        labels = torch.randint(0, 1000, (1024,), generator=torch.Generator().manual_seed(5))[n_img[0]:n_img[1]].to(dev)
-        noise = torch.randn(1024, 3, 256, 256, generator=torch.Generator().manual_seed(6))[n_img[0]:n_img[1]].to(dev)
-        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
-        from flowmatching_lthc.sampling import sample_heun as sample_ref
-        state = {"installed": True}
+        for _ in range(3):
+            train()
+        ms = _timed(train, 10, stream)
+        leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
+        del net, opt
+    out["train_step"] = {"config": "BASELINE config 4: fwd+bwd+AdamW, 32 images per GPU, bf16 autocast" +
+                         (f", DDP over {r.world} GPUs" if r.world > 1 else ""), "batch_per_gpu": B, "steps": 10,
+                         **leg.pop("ours"), **({"reference_gpu": leg["reference"]} if leg else {})}
+    # the training step changed the weights: sample with fresh ones
+    m = _model(dev)
+    if refm is not None:
+        refm = _reference_model(dev)
 
-        def step(n_steps=50):
-            with torch.autocast("cuda", dtype=torch.bfloat16):
-                if state["installed"]:
-                    sample_doubled(m, labels, steps=n_steps, cfg_scale=1.5, noise=noise, prediction="velocity")
-                else:
-                    torch.manual_seed(6)
-                    sample_ref(m, labels, steps=n_steps, cfg_scale=1.5, prediction="velocity")
-        per_step, warm, steps = nb, 1, max(1, min(args.steps, 2))
+    # config 5: Heun-50 CFG sampling of 1024 images sharded over the ranks
+    lo, hi = D.shard(SAMPLE_IMAGES, r.rank, r.world)
+    n = hi - lo
+    labels_all = torch.randint(0, 1000, (SAMPLE_IMAGES,), generator=torch.Generator().manual_seed(5))
+    chunks = [(a, min(a + SAMPLE_CHUNK, hi)) for a in range(lo, hi, SAMPLE_CHUNK)]
+    noise = {c: image_noise(6, *c).pin_memory() for c in chunks}
+    kw = dict(steps=50, cfg_scale=1.5, num_classes=1000, prediction="velocity")
+    m.eval()
+    samplers = {}
+    for a, b in chunks:
+        if b - a not in samplers:
+            samplers[b - a] = GraphedHeunSampler(m, b - a, device=dev, **kw)
+    outs = {c: torch.empty(c[1] - c[0], 3, 256, 256, pin_memory=True) for c in chunks}
 
-    def timed(installed: bool) -> float:
-        handle = integration.install(Lm) if installed else None
-        if op == "sample":
-            state["installed"] = installed
-            step(2)  # warm-up: compiles the reference's Triton op, fills the allocator
-        else:
-            for _ in range(warm):
-                step()
-        torch.cuda.synchronize()
-        D.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            step()
-        e1.record(stream)
-        e1.synchronize()
-        D.barrier()
-        if handle:
-            handle.uninstall()
-        return D.reduce_max(e0.elapsed_time(e1), dev)
+    def sample():
+        for c in chunks:
+            img = samplers[c[1] - c[0]](labels_all[c[0]:c[1]].to(dev, non_blocking=True), noise[c].to(dev, non_blocking=True))
+            outs[c].copy_(img, non_blocking=True)
+    ms = _timed(sample, 1, stream)
+    leg = {"images_per_s": round(SAMPLE_IMAGES / (ms / 1e3), 2), "ms": round(ms, 1)}
+    if refm is not None:
+        from flowmatching_lthc.sampling import sample_heun as ref_sample_heun
 
-    ms_ours = timed(True)
-    total = (1024 if op == "sample" else per_step * r.world) * steps
-    out = {"ms_ours": ms_ours, "images": total, "steps": steps, "value": total / (ms_ours / 1e3)}
-    # The reference's fused materialisation (Triton, local_thc_triton_kernels.py:317-405)
-    # computes element offsets in 32-bit integers; at the B/4 shape they wrap for a
-    # model call with more than REF_TRITON_MAX_BATCH images, and running it there
-    # raised an illegal memory access on this pool.  Its GPU path is not run there.
-    ref_batch = per_step  # images per model call in the reference arm
-    if ref_batch > REF_TRITON_MAX_BATCH:
-        out["ref_unavailable"] = (f"reference Triton materialise op overflows 32-bit offsets for more than "
-                                  f"{REF_TRITON_MAX_BATCH} images per call (this call: {ref_batch}); not run")
-    else:
-        ms_ref = timed(False)
-        out.update(ms_ref=ms_ref, ref_value=total / (ms_ref / 1e3))
+        refm.eval()
+
+        def ref_sample():
+            for a0 in range(lo, hi, 256):
+                b0 = min(a0 + 256, hi)
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    ref_sample_heun(refm, labels_all[a0:b0].to(dev), **kw)
+        ms = _timed(ref_sample, 1, stream)
+        leg["reference_gpu"] = {"images_per_s": round(SAMPLE_IMAGES / (ms / 1e3), 2), "ms": round(ms, 1),
+                                "path": "reference two-call CFG sampler, eager LTHC + Triton materialisation, "
+                                        "chunks of 256 images"}
+    out["sample"] = {"config": "BASELINE config 5: Heun-50, CFG 1.5, 1024 images of 256x256, bf16 autocast",
+                     "images": SAMPLE_IMAGES, "images_per_gpu": n, "chunk": SAMPLE_CHUNK,
+                     "path": "doubled-batch CFG, whole loop of each chunk replayed as one CUDA graph, "
+                             "host-seeded per-image noise (pinned) copied in, images copied out",
+                     **leg}
+    del samplers
     return out
 
+
+def _reference_model(dev):
+    """The reference's own released model class with the same seeded weights as _model
+    (needs the reference package importable: LTHC_REFERENCE or baseline/_ref)."""
+    for cand in (os.environ.get("LTHC_REFERENCE"), str(ROOT / "baseline" / "_ref")):
+        if cand and (Path(cand) / "flowmatching_lthc").exists() and cand not in sys.path:
+            sys.path.insert(0, cand)
+    from flowmatching_lthc.models import build_model as ref_build
+
+    from flowmatching_lthc_b200.model import fill_seeded_
+
+    return fill_seeded_(ref_build("lthc_b4_velocity"), 1).to(dev)
 
 
 # ------------------------------------------------------------------ reference arm
@@ -416,6 +507,9 @@ def reference_arm(args, r: D.Rank) -> int:
                          "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    eager = reference_eager_cpu(Bs, 5.0)
+    if eager is not None:
+        line["reference_eager_cpu"] = eager
     print(json.dumps(line), flush=True)
     return 0
 
@@ -485,31 +579,6 @@ def main() -> int:
     stream = torch.cuda.current_stream(dev)
     B = args.batch
 
-    if args.op in MODEL_OPS:
-        res = model_bench(args, r, dev, stream)
-        if r.is_main:
-            cfg_model = {"workload": {"model_fwd": "LTHC-B/4 random-init forward, BASELINE config 3",
-                                      "train_step": "LTHC-B/4 velocity training step fwd+bwd+AdamW, BASELINE config 4",
-                                      "sample": "Heun-50 CFG 1.5 sampling of 1024 images, BASELINE config 5"}[args.op],
-                         "op": args.op, "model": "lthc_b4_velocity (reference code, random init)",
-                         "batch_per_gpu": {"model_fwd": B, "train_step": 32}.get(args.op, 1024 // r.world),
-                         "image_size": 256, "dtype": "bf16 autocast", "parallelism": f"dp{r.world}"}
-            print(json.dumps({
-                "metric": "LTHC-B/4 images/sec", "value": round(res["value"], 2), "unit": "images/s",
-                "n_gpus": r.world, "steps": res["steps"], "warmup": args.warmup,
-                "ms_per_step": round(res["ms_ours"] / res["steps"], 3), "higher_is_better": True,
-                "scaling": "strong" if args.op == "sample" else "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic images/noise/labels, random-init weights", "config": cfg_model,
-                "reference_gpu": ({"value": round(res["ref_value"], 2), "unit": "images/s",
-                                   "ms_per_step": round(res["ms_ref"] / res["steps"], 3),
-                                   "path": "reference eager LTHC + Triton materialise (uninstalled)"}
-                                  if "ref_value" in res else {"unavailable": res["ref_unavailable"]}),
-                "speedup_vs_reference_gpu": (round(res["value"] / res["ref_value"], 4) if "ref_value" in res
-                                             else None)}), flush=True)
-        D.barrier()
-        D.shutdown()
-        return 0
-
     cfg = _op_inputs(B, dev, seed=1000 + r.rank)
     step, bytes_step, launches, kernel = op_step(args.op, cfg)
     step()
@@ -562,13 +631,21 @@ def main() -> int:
         e2e_step()
         torch.cuda.synchronize()
         n_e2e = max(3, min(args.steps, 10))
+        D.barrier()
         e2e_ms = D.reduce_max(time_device(e2e_step, n_e2e, stream), dev)
         h2d = h_x0.numel() * 2 + sum(d.numel() * 2 for d in h_dz)
+        d2h = h_out.numel() * 2
+        link = host_link(h_x0, x0, r, dev, stream)
+        bound_ms = max(h2d / link["h2d_gbs"], d2h / link["d2h_gbs"]) / 1e6
         e2e = {"value": round(r.world * bytes_step / (e2e_ms / 1e3) / 1e9, 3), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h_out.numel() * 2,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(e2e_ms, 3), "steps": n_e2e,
                "path": ("pinned host buffers -> chunked cudaMemcpyAsync in / lthc_b200::materialise (C ABI) / "
-                        "copy out on three streams (HostMaterialiser, 8-image chunks) -> host")}
+                        "copy out on three streams (HostMaterialiser, 8-image chunks) -> host"),
+               "host_link": {**link, "copy_bound_ms": round(bound_ms, 3),
+                             "frac_of_copy_bound": round(bound_ms / e2e_ms, 3),
+                             "note": (f"pinned copies measured with all {r.world} ranks copying at once; the bound "
+                                      "assumes the two directions fully overlap")}}
         del h_x0, h_dz, h_out, hm
 
     extras = {}
@@ -594,6 +671,11 @@ def main() -> int:
         line["comparators"] = extras.get("comparators")
         if "materialise_final_clusters" in extras:
             line["materialise_final_clusters"] = extras["materialise_final_clusters"]
+    if args.op == "materialise_fwd" and not args.no_model:
+        del cfg, step, extras
+        torch.cuda.empty_cache()
+        line["images_per_s"] = model_legs(r, dev, stream, reference_gpu=args.reference_gpu)
+        line["gpu_launches_note"] = "gpu_launches counts the headline materialisation steps only"
     if r.is_main and r.world == 1 and args.op == "materialise_fwd":
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if r.is_main:

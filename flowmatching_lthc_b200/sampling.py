@@ -105,8 +105,8 @@ class GraphedHeunSampler:
     until the next call; ``clone()`` it to keep it).  `autocast` is the dtype the
     model runs under (None: no autocast).  The model's weights are read in place at
     every replay, so parameter updates are seen; shapes, the step count and the
-    guidance settings are fixed at capture.  Capture runs one eager warm-up of the
-    loop first (library workspaces, allocator pools)."""
+    guidance settings are fixed at capture.  Capture is preceded by one eager model
+    call at the doubled batch (library handles and workspaces)."""
 
     def __init__(self, model, batch: int, *, image_size=256, noise_scale=1.0, steps=50, cfg_scale=1.0,
                  interval=(0.0, 1.0), num_classes=1000, t_eps=5e-2, prediction="clean",
@@ -123,17 +123,20 @@ class GraphedHeunSampler:
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side):
-            self._run()  # warm-up outside the capture
+            self._run(warm_up=True)  # one model call outside the capture: library handles, workspaces
         torch.cuda.current_stream(device).wait_stream(side)
         torch.cuda.synchronize(device)
         with torch.cuda.graph(self.graph):
             self.out = self._run()
 
     @torch.no_grad()
-    def _run(self) -> torch.Tensor:
+    def _run(self, warm_up: bool = False) -> torch.Tensor:
         ctx = (torch.autocast("cuda", dtype=self.autocast) if self.autocast is not None
                else contextlib.nullcontext())
         with ctx:
+            if warm_up:
+                t = torch.full((self.batch, 1, 1, 1), float(self.ts[0]), device=self.noise.device)
+                return cfg_velocity_doubled(self.model, self.noise, t, self.labels, **self.kw)
             return _heun_loop(self.model, self.noise * self.noise_scale, self.labels, self.ts, self.kw)
 
     def __call__(self, labels: torch.Tensor, noise: torch.Tensor) -> torch.Tensor:
