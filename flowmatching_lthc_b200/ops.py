@@ -294,6 +294,62 @@ def _(grad_out, dz, beta, need_grad_dz, need_grad_beta):
     return gdz, gbeta
 
 
+@_custom_op("materialise_grad_dz")
+def materialise_grad_dz(grad_out: Tensor, beta: list[Tensor]) -> list[Tensor]:
+    """grad_dz_l = sum_r beta_l grad_out per cell, alone: the weight-gradient half is
+    not run and no update tensor is needed (the C call gets NULL for them)."""
+    L = len(beta)
+    if L < 1 or L > MAX_LAYERS:
+        raise ValueError(f"materialise_grad_dz: need 1..{MAX_LAYERS} betas, got {L}")
+    _require_cuda(grad_out, *beta)
+    b, g, c = _hi_geom(grad_out, "materialise_grad_dz")
+    for w in beta:
+        _check_weight(w, c, "materialise_grad_dz")
+    grad_out = grad_out.contiguous()
+    beta = [w.to(beta[0].dtype).contiguous() for w in beta]
+    gdz = [torch.empty((b, g * g, c), device=grad_out.device, dtype=grad_out.dtype) for _ in range(L)]
+    with _guard(grad_out):
+        _lib.call("lthc_materialise_bwd", grad_out.data_ptr(), None, _lib.ptr_array([w.data_ptr() for w in beta]),
+                  _code(beta[0], "materialise_grad_dz"), L, _lib.ptr_array([t.data_ptr() for t in gdz]), None,
+                  None, 0, b, g, c, _code(grad_out, "materialise_grad_dz"), _stream(grad_out))
+    return gdz
+
+
+@materialise_grad_dz.register_fake
+def _(grad_out, beta):
+    b, h, _, c = grad_out.shape
+    return [grad_out.new_empty((b, (h // 4) ** 2, c)) for _ in beta]
+
+
+@_custom_op("materialise_grad_beta")
+def materialise_grad_beta(grad_out: Tensor, dz: list[Tensor]) -> Tensor:
+    """grad_beta [L,C,16] fp32 = sum over cells of grad_out * dz_l, alone: no write
+    weights are needed (the C call gets NULL for them)."""
+    L = len(dz)
+    if L < 1 or L > MAX_LAYERS:
+        raise ValueError(f"materialise_grad_beta: need 1..{MAX_LAYERS} updates, got {L}")
+    _require_cuda(grad_out, *dz)
+    b, g, c = _hi_geom(grad_out, "materialise_grad_beta")
+    for t in dz:
+        if tuple(t.shape) != (b, g * g, c):
+            raise ValueError(f"materialise_grad_beta: every dz must be [{b},{g * g},{c}], got {tuple(t.shape)}")
+    grad_out = grad_out.contiguous()
+    dz = [t.to(grad_out.dtype).contiguous() for t in dz]
+    gbeta = torch.empty((L, c, 16), device=grad_out.device, dtype=torch.float32)
+    with _guard(grad_out):
+        ws_bytes = _lib.load().lthc_materialise_bwd_workspace_bytes(b, g, c, L)
+        ws = _workspace(ws_bytes, grad_out.device)
+        _lib.call("lthc_materialise_bwd", grad_out.data_ptr(), _lib.ptr_array([t.data_ptr() for t in dz]), None,
+                  _lib.DTYPE_F32, L, None, gbeta.data_ptr(), ws.data_ptr(), ws_bytes, b, g, c,
+                  _code(grad_out, "materialise_grad_beta"), _stream(grad_out))
+    return gbeta
+
+
+@materialise_grad_beta.register_fake
+def _(grad_out, dz):
+    return grad_out.new_empty((len(dz), grad_out.shape[-1], 16), dtype=torch.float32)
+
+
 def _materialise_setup(ctx, inputs, output):
     x0, dz, beta = inputs
     ctx.save_for_backward(*dz, *beta)
@@ -925,17 +981,16 @@ def final_accumulate_b4_traceable(x0: Tensor, dz_stack: Tensor, beta_stack: Tens
 
 def final_accumulate_b4_12_grad_dz_ptr_traceable(grad_out: Tensor, *betas: Tensor) -> Tensor:
     """jit_thc::final_accumulate_b4_12_grad_dz_ptr -> [12,B,256,C] (:1800-1845)."""
-    dummy = [grad_out.new_empty((grad_out.shape[0], (grad_out.shape[1] // 4) ** 2, grad_out.shape[3]))] * len(betas)
-    gdz, _ = materialise_bwd(grad_out, dummy, list(betas), True, False)
-    return torch.stack(gdz)
+    if len(betas) != 12:
+        raise ValueError(f"expected 12 beta tensors, got {len(betas)}")
+    return torch.stack(materialise_grad_dz(grad_out, list(betas)))
 
 
 def final_accumulate_b4_12_grad_beta_ptr_traceable(grad_out: Tensor, *dzs: Tensor) -> Tensor:
     """jit_thc::final_accumulate_b4_12_grad_beta_ptr -> [12,C,16] fp32 (:1848-1894)."""
-    c = grad_out.shape[-1]
-    dummy = [grad_out.new_empty((c, 16), dtype=torch.float32)] * len(dzs)
-    _, gbeta = materialise_bwd(grad_out, list(dzs), dummy, False, True)
-    return gbeta
+    if len(dzs) != 12:
+        raise ValueError(f"expected 12 dz tensors, got {len(dzs)}")
+    return materialise_grad_beta(grad_out, list(dzs))
 
 
 def local_write_traceable(x: Tensor, weight: Tensor) -> Tensor:
@@ -959,7 +1014,8 @@ def local_weight_grad_traceable(high: Tensor, low: Tensor) -> Tensor:
 
 
 __all__ = [
-    "read", "read_bwd", "write", "write_bwd", "write_add", "materialise", "materialise_bwd", "lazy_update",
+    "read", "read_bwd", "write", "write_bwd", "write_add", "materialise", "materialise_bwd", "materialise_grad_dz",
+    "materialise_grad_beta", "lazy_update",
     "lazy_update_bwd", "weight_grad", "final_accumulate_b4_12_traceable", "final_accumulate_b4_traceable",
     "final_accumulate_b4_12_grad_dz_ptr_traceable", "final_accumulate_b4_12_grad_beta_ptr_traceable",
     "local_write_traceable", "local_read_traceable", "local_read_add_traceable", "local_weight_grad_traceable",

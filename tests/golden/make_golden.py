@@ -3,7 +3,7 @@ reference's own eager PyTorch code (tongtongliang/flowmatching_lthc) on CPU.
 
 Run from the repository root with the reference importable, e.g.
 
-    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py [all|lthc|final|branch]
+    LTHC_REFERENCE=/path/to/flowmatching_lthc python tests/golden/make_golden.py [all|lthc|final|branch|config1]
 
 The reference is only needed to (re)generate the fixtures; the committed ``*.pt``
 files are what the tests read.  Every tensor is produced by the reference
@@ -225,8 +225,38 @@ CASES = [
 ]
 
 
+# BASELINE configuration 1 exactly (B = 2, 16x16 workspace, C = 768, fp32, R used as
+# alpha without the softmax, seed 0), inputs from flowmatching_lthc_b200.workloads.config1.
+# The residual-sized outputs are 25 MB each, so a fixed sample of positions is kept.
+CONFIG1_SAMPLE_STRIDE = 97
+
+
+def make_config1_case(name: str) -> dict:
+    sys.path.insert(0, str(HERE.parent.parent))
+    from flowmatching_lthc_b200 import workloads as W
+
+    cfg = W.config1()
+    B, G, C = cfg["B"], cfg["G"], cfg["C"]
+    hi = 4 * G
+    read = L.SharedLocalRead(hi, G, C, C, use_softmax_write=False)
+    read.read_logits.data.copy_(cfg["R"])
+    write = L.LayerLocalWrite(hi, G, C, C)
+    write.write_weight.data.copy_(cfg["P"])
+    with torch.no_grad():
+        z = read.read(cfg["x"])
+        wa = write.write_add(cfg["x"], cfg["dz"])
+        w = write.write(cfg["dz"])
+    idx = torch.arange(0, wa.numel(), CONFIG1_SAMPLE_STRIDE)
+    return {"meta": {"name": name, "B": B, "G": G, "C": C, "dtype": "torch.float32", "seed": 0,
+                     "sample_stride": CONFIG1_SAMPLE_STRIDE},
+            "read_z": z, "write_add_sample": wa.reshape(-1)[idx].clone(), "write_sample": w.reshape(-1)[idx].clone(),
+            "write_add_sum": wa.double().sum().item(), "read_z_sum": z.double().sum().item()}
+
+
 def main(which: str = "all") -> None:
     jobs = []
+    if which in ("all", "config1"):
+        jobs += [("config1_b2_c768_f32", lambda name: make_config1_case(name), {})]
     if which in ("all", "lthc"):
         jobs += [(name, make_case, kw) for name, kw in CASES]
     if which in ("all", "final"):
