@@ -64,8 +64,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                   _L, _I, _P]),
     "lthc_patch_embed_read_fwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _L, _I, _L, _L, _P]),
     "lthc_final_norm_modulate_fwd": (_I, [_P, _P, _I, _P, _P, _L, _P, _L, _L, _L, c_float, _I, _P]),
-    "lthc_materialise_final_fwd": (_I, [_P, _PP, _PP, _I, _I, _P, _I, _P, _P, _L, c_float, _P, _L, _L, _L, _I, _P]),
-    "lthc_materialise_final_supported": (_I, [_L, _I, _I, POINTER(c_int)]),
     "lthc_final_norm_modulate_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
     "lthc_final_norm_modulate_bwd": (_I, [_P, _P, _I, _P, _L, _P, _P, _P, _P, _P, _P, c_size_t, _L, _L, _L,
                                           c_float, _I, _P]),

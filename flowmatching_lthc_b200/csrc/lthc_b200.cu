@@ -22,7 +22,6 @@
 #include "lthc_umma.cuh"
 #include "lthc_embed.cuh"
 #include "lthc_branch.cuh"
-#include "lthc_matfinal.cuh"
 
 namespace lthc {
 
@@ -324,134 +323,6 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
 }
 
 // ---- materialisation fused with the final norm + modulate (clusters) ----------
-
-// Clusters of `cluster` CTAs of this kernel and launch shape that can be resident
-// at once on the current device (cached); the kernel is opted in to its dynamic
-// shared memory and, above 8 CTAs, to non-portable cluster sizes.  0 when no
-// such cluster fits.
-template <typename Kernel>
-int cluster_capacity(Kernel kern, int threads, int smem_bytes, int cluster, int* out) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int, int>, int> cache;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return launched("cudaGetDevice");
-  const void* fn = reinterpret_cast<const void*>(kern);
-  const auto key = std::make_tuple(dev, fn, smem_bytes, cluster);
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(key);
-  if (it == cache.end()) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
-      return launched("cudaFuncSetAttribute (shared memory)");
-    if (cluster > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-      return launched("cudaFuncSetAttribute (cluster size)");
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = static_cast<unsigned>(cluster);
-    at[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(1, static_cast<unsigned>(cluster));
-    cfg.blockDim = dim3(static_cast<unsigned>(threads));
-    cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
-      cudaGetLastError();
-      n = 0;
-    }
-    it = cache.emplace(key, n).first;
-  }
-  *out = it->second;
-  return LTHC_OK;
-}
-
-template <typename T, int LT>
-int launch_matfinal(MatFinalParams& q, cudaStream_t s, bool query_only, int* capacity) {
-  using Lay = MatFinalLayout<T, LT>;
-  constexpr int kThreads = BcastShape<LT, true>::kThreads;
-  auto kern = materialise_final_kernel<T, LT>;
-  const int64_t slices = slices_of(q.m.C);
-  int nclusters = 0;
-  LTHC_TRY(cluster_capacity(kern, kThreads, Lay::kSmemBytes, static_cast<int>(slices), &nclusters));
-  if (capacity) *capacity = nclusters;
-  if (query_only) return LTHC_OK;
-  if (nclusters < 1)
-    return fail(LTHC_ERR_LAUNCH, "a cluster of %lld CTAs of the fused materialisation cannot be scheduled here",
-                (long long)slices);
-  int64_t nx = std::max<int64_t>(1, std::min<int64_t>(nclusters, q.m.strips));
-  q.m.strips_per_cta = ceil_div(q.m.strips, nx);
-  nx = ceil_div(q.m.strips, q.m.strips_per_cta);
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = 1;
-  at[0].val.clusterDim.y = static_cast<unsigned>(slices);
-  at[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Lay::kSmemBytes;
-  cfg.stream = s;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return fail(LTHC_ERR_LAUNCH, "materialise + final norm (cluster) launch failed: %s", cudaGetErrorString(e));
-  }
-  return launched("materialise + final norm (cluster)");
-}
-
-template <typename T>
-int matfinal_t(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype, int L,
-               const void* norm_w, int norm_w_dtype, const void* shift, const void* scale, int64_t mod_stride,
-               float eps, void* out, int64_t B, int64_t G, int64_t C, cudaStream_t s, bool query_only,
-               int* capacity) {
-  MatFinalParams q;
-  memset(&q, 0, sizeof(q));
-  BcastTmaParams& p = q.m;
-  if (!query_only) {
-    LTHC_TRY(encode_residual_map<T>(&p.tm_base, x0, B, G, C));
-    LTHC_TRY(encode_residual_map<T>(&p.tm_out, out, B, G, C));
-    for (int l = 0; l < L; ++l) {
-      LTHC_TRY(encode_workspace_map<T>(&p.tm_dz[l], dz[l], B * G * G, C));
-      p.w[l] = beta[l];
-    }
-  }
-  p.out = out;
-  p.w_dtype = beta_dtype;
-  p.L = L;
-  p.G = static_cast<int>(G);
-  p.strips_per_row = static_cast<int>(ceil_div(G, kStripCells));
-  p.C = C;
-  p.strips = B * G * p.strips_per_row;
-  q.norm_w = norm_w;
-  q.norm_w_dtype = norm_w_dtype;
-  q.shift = shift;
-  q.scale = scale;
-  q.eps = eps;
-  q.inv_c = 1.0f / static_cast<float>(C);
-  q.mod_stride = mod_stride;
-  return L == 12 ? launch_matfinal<T, 12>(q, s, query_only, capacity)
-                 : launch_matfinal<T, 0>(q, s, query_only, capacity);
-}
-
-int matfinal(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype, int L,
-             const void* norm_w, int norm_w_dtype, const void* shift, const void* scale, int64_t mod_stride, float eps,
-             void* out, int64_t B, int64_t G, int64_t C, int act, cudaStream_t s, bool query_only, int* capacity) {
-  switch (act) {
-    case LTHC_DTYPE_F32:
-      return matfinal_t<float>(x0, dz, beta, beta_dtype, L, norm_w, norm_w_dtype, shift, scale, mod_stride, eps, out,
-                               B, G, C, s, query_only, capacity);
-    case LTHC_DTYPE_BF16:
-      return matfinal_t<__nv_bfloat16>(x0, dz, beta, beta_dtype, L, norm_w, norm_w_dtype, shift, scale, mod_stride,
-                                       eps, out, B, G, C, s, query_only, capacity);
-    default:
-      return matfinal_t<__half>(x0, dz, beta, beta_dtype, L, norm_w, norm_w_dtype, shift, scale, mod_stride, eps, out,
-                                B, G, C, s, query_only, capacity);
-  }
-}
-
 // ---- read family -------------------------------------------------------------
 struct ReadJob {
   const void* h;               // residual-sized input
@@ -546,21 +417,6 @@ int read_family(const ReadJob& j, size_t ws_bytes, int act, cudaStream_t s) {
 
 int check_weight_dtype(int dt, const char* name) {
   if (!valid_act(dt)) return fail(LTHC_ERR_DTYPE, "unknown %s dtype code %d", name, dt);
-  return LTHC_OK;
-}
-
-int check_matfinal(int64_t B, int64_t G, int64_t C, int n_layers, int act, int beta_dtype, int norm_w_dtype,
-                   int64_t mod_stride, float eps) {
-  LTHC_TRY(check_geometry(B, G, C, act));
-  LTHC_TRY(check_weight_dtype(beta_dtype, "beta"));
-  LTHC_TRY(check_weight_dtype(norm_w_dtype, "norm weight"));
-  LTHC_TRY(check_layers(n_layers));
-  if (C > static_cast<int64_t>(kSliceCh) * kMatFinalMaxSlices)
-    return fail(LTHC_ERR_SHAPE, "channels must be <= %d for the fused final norm, got %lld",
-                kSliceCh * kMatFinalMaxSlices, (long long)C);
-  if (mod_stride < C) return fail(LTHC_ERR_SHAPE, "shift/scale row stride %lld is below C = %lld",
-                                  (long long)mod_stride, (long long)C);
-  if (!(eps >= 0.f)) return fail(LTHC_ERR_SHAPE, "eps must be >= 0");
   return LTHC_OK;
 }
 
@@ -1351,42 +1207,6 @@ int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight, int w_d
         p.partial, grad_weight, grad_shift, grad_scale, B, K, C);
     LTHC_TRY(launched("final norm/modulate backward finalize"));
   }
-  return LTHC_OK;
-}
-
-// ------------- materialisation fused with the final norm + modulate -------------
-
-int lthc_materialise_final_fwd(const void* x0, const void* const* dz, const void* const* beta, int beta_dtype,
-                               int n_layers, const void* norm_weight, int norm_weight_dtype, const void* shift,
-                               const void* scale, int64_t mod_stride, float eps, void* m_out, int64_t B, int64_t G,
-                               int64_t C, int act_dtype, void* stream) {
-  LTHC_TRY(check_matfinal(B, G, C, n_layers, act_dtype, beta_dtype, norm_weight_dtype, mod_stride, eps));
-  if (!dz || !beta) return fail(LTHC_ERR_NULL_POINTER, "dz / beta pointer arrays are NULL");
-  LTHC_TRY(check_act(x0, "x0", B > 0));
-  LTHC_TRY(check_act(m_out, "m_out", B > 0));
-  LTHC_TRY(check_ptr(norm_weight, "norm_weight"));
-  if (B > 0 && (!shift || !scale)) return fail(LTHC_ERR_NULL_POINTER, "shift / scale is NULL");
-  for (int l = 0; l < n_layers; ++l) {
-    LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
-    LTHC_TRY(check_ptr(beta[l], "beta[l]"));
-  }
-  if (B == 0) return LTHC_OK;
-  int sms = 0;
-  LTHC_TRY(current_device(&sms));
-  return matfinal(x0, dz, beta, beta_dtype, n_layers, norm_weight, norm_weight_dtype, shift, scale, mod_stride, eps,
-                  m_out, B, G, C, act_dtype, static_cast<cudaStream_t>(stream), false, nullptr);
-}
-
-int lthc_materialise_final_supported(int64_t C, int n_layers, int act_dtype, int* clusters) {
-  if (!clusters) return fail(LTHC_ERR_NULL_POINTER, "clusters is NULL");
-  *clusters = 0;
-  LTHC_TRY(check_matfinal(1, 16, C, n_layers, act_dtype, LTHC_DTYPE_F32, LTHC_DTYPE_F32, C, 0.f));
-  int sms = 0;
-  LTHC_TRY(current_device(&sms));
-  int cap = 0;
-  LTHC_TRY(matfinal(nullptr, nullptr, nullptr, LTHC_DTYPE_F32, n_layers, nullptr, LTHC_DTYPE_F32, nullptr, nullptr, C,
-                    0.f, nullptr, 1, 16, C, act_dtype, nullptr, true, &cap));
-  *clusters = cap;
   return LTHC_OK;
 }
 

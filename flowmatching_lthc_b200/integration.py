@@ -18,8 +18,7 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
   SharedReadLocalTHCSharedAdaLNJiT.forward_lazy (patch embedding + shared read
       fused on the tensor cores under bf16 autocast; each block's branch
-      epilogue, :318-323, fused with its lazy update; with FUSE_FINAL and no
-      autograd, the materialisation and the final norm + modulate as one kernel) :1374-1388
+      epilogue, :318-323, fused with its lazy update)                  :1374-1388
 
 Shape checks and messages are the reference's own; the arithmetic runs in
 ``liblthc_b200.so``.  The patched methods accept CUDA tensors only (a CPU tensor
@@ -155,43 +154,9 @@ def _forward_lazy(self, x: torch.Tensor, t: torch.Tensor, y: torch.Tensor) -> to
     for block in self.blocks:
         dz, z = _branch_and_update(block, z, t6, self.workspace_rope, self.shared_read)
         updates.append(dz)
-    fl = self.final_layer
-    if (FUSE_FINAL and not torch.is_grad_enabled() and type(fl).forward is _final_layer and x0.dtype == t2.dtype
-            and ops.materialise_final_supported(x0, len(updates))):
-        betas = _accumulate_betas(self, x0, updates)
-        if betas is not None:
-            # inference: materialisation + final RMSNorm + modulate in one pass (X_L stays on chip)
-            shift, scale = t2.chunk(2, dim=1)
-            m = ops.call(ops.materialise_final, x0, updates, betas, fl.norm_final.weight, shift, scale,
-                         fl.norm_final.eps)
-            b, hh, wh, c_dim = m.shape
-            return self.unpatchify(fl.linear(m.reshape(b, hh * wh, c_dim)))
     x_hi = self.final_accumulate_reference(x0, updates)
     b, hh, wh, c_dim = x_hi.shape
     return self.unpatchify(self.final_layer(x_hi.reshape(b, hh * wh, c_dim), t2))
-
-
-# True: the inference forward runs the materialisation fused with the final norm +
-# modulate (lthc_materialise_final_fwd) instead of the two calls.  Off by default:
-# on B200 the fused kernel (0.51 ms at B = 64) is slower than the two kernels it
-# replaces (0.20 + 0.17 ms); its outputs equal theirs.
-FUSE_FINAL = False
-
-
-def _accumulate_betas(model, x0: torch.Tensor, updates: list[torch.Tensor]) -> list[torch.Tensor] | None:
-    """The betas the installed final_accumulate_reference of the model's class
-    passes to the materialisation, or None when that method is not one of ours."""
-    fn = type(model).final_accumulate_reference
-    c = x0.shape[-1]
-    if fn is _final_loop:
-        if len(updates) != len(model.blocks):
-            return None
-        return [per_channel(b.write.beta(dtype=d.dtype), c) for b, d in zip(model.blocks, updates)]
-    if fn is _final_stacked or fn is _final12:
-        if len(updates) != len(model.blocks) or (fn is _final12 and len(updates) != 12):
-            return None
-        return [per_channel(b.write.write_weight, c) for b in model.blocks]
-    return None
 
 
 PATCHES = (

@@ -884,82 +884,6 @@ def _final_backward(ctx, grad_out):
 final_norm_modulate.register_autograd(_final_backward, setup_context=_final_setup)
 
 
-# ---------------------------------------------------------------------------
-# materialisation fused with the final norm + modulate (inference)
-# ---------------------------------------------------------------------------
-_MATFINAL_SUPPORT: dict = {}
-
-
-def materialise_final_supported(x0: Tensor, n_layers: int) -> bool:
-    """Whether the fused kernel takes this residual: CUDA, C <= 1024 and a
-    multiple of 8, 1..12 layers, and the device can schedule its clusters of
-    ceil(C/64) CTAs (queried once per device, C, layer count and dtype)."""
-    if x0.device.type != "cuda" or x0.dim() != 4 or x0.dtype not in _DTYPE_CODE:
-        return False
-    c = x0.shape[-1]
-    if c % 8 != 0 or c < 8 or c > FINAL_MAX_CHANNELS or not 1 <= n_layers <= MAX_LAYERS:
-        return False
-    key = (x0.device.index, c, n_layers, x0.dtype)
-    if key not in _MATFINAL_SUPPORT:
-        flag = ctypes.c_int(0)
-        with _guard(x0):
-            _lib.call("lthc_materialise_final_supported", c, n_layers, _DTYPE_CODE[x0.dtype], ctypes.byref(flag))
-        _MATFINAL_SUPPORT[key] = int(flag.value)
-    return _MATFINAL_SUPPORT[key] > 0
-
-
-def materialise_final_clusters(x0: Tensor, n_layers: int) -> int:
-    """How many clusters of the fused kernel the device holds at once (0: none)."""
-    return _MATFINAL_SUPPORT[(x0.device.index, x0.shape[-1], n_layers, x0.dtype)] if materialise_final_supported(
-        x0, n_layers) else 0
-
-
-@_custom_op("materialise_final")
-def materialise_final(x0: Tensor, dz: list[Tensor], beta: list[Tensor], norm_weight: Tensor, shift: Tensor,
-                      scale: Tensor, eps: float) -> Tensor:
-    """modulate(RMSNorm(X_L), shift, scale) with X_L = X_0 + sum_l beta_l (.) dz_l, in
-    one pass that never writes X_L (inference; no autograd formula).  Output
-    [B, 4G, 4G, C] in x0's dtype; shift / scale [B, C] in that dtype."""
-    L = len(dz)
-    if L < 1 or L > MAX_LAYERS or len(beta) != L:
-        raise ValueError(f"materialise_final: need 1..{MAX_LAYERS} layers with one beta each, got {L} / {len(beta)}")
-    _require_cuda(x0, *dz, *beta, norm_weight, shift, scale)
-    b, g, c = _lo_geom(dz[0], "materialise_final")
-    if c > FINAL_MAX_CHANNELS:
-        raise ValueError(f"materialise_final: channel count {c} above {FINAL_MAX_CHANNELS}")
-    act = x0.dtype
-    if tuple(x0.shape) != (b, 4 * g, 4 * g, c):
-        raise ValueError(f"materialise_final: expected x0 [{b},{4 * g},{4 * g},{c}], got {tuple(x0.shape)}")
-    for t in dz:
-        if tuple(t.shape) != (b, g * g, c):
-            raise ValueError(f"materialise_final: every dz must be [{b},{g * g},{c}], got {tuple(t.shape)}")
-    for w in beta:
-        _check_weight(w, c, "materialise_final")
-    if tuple(norm_weight.shape) != (c,):
-        raise ValueError(f"materialise_final: expected norm weight [{c}], got {tuple(norm_weight.shape)}")
-    for name, m in (("shift", shift), ("scale", scale)):
-        if tuple(m.shape) != (b, c):
-            raise ValueError(f"materialise_final: expected {name} [{b},{c}], got {tuple(m.shape)}")
-        if m.dtype != act:
-            raise ValueError(f"materialise_final: {name} dtype {m.dtype} differs from the activation dtype {act}")
-    wdt = beta[0].dtype
-    x0 = x0.contiguous()
-    dz = [t.to(act).contiguous() for t in dz]
-    beta = [w.to(wdt).contiguous() for w in beta]
-    norm_weight = norm_weight.contiguous()
-    sh, sc, stride = _mod_rows(shift, scale)
-    out = torch.empty_like(x0)
-    with _guard(out):
-        _lib.call("lthc_materialise_final_fwd", x0.data_ptr(), _lib.ptr_array([t.data_ptr() for t in dz]),
-                  _lib.ptr_array([w.data_ptr() for w in beta]), _code(beta[0], "materialise_final"), L,
-                  norm_weight.data_ptr(), _code(norm_weight, "norm weight"), sh.data_ptr(), sc.data_ptr(), stride,
-                  float(eps), out.data_ptr(), b, g, c, _code(out, "materialise_final"), _stream(out))
-    return out
-
-
-@materialise_final.register_fake
-def _(x0, dz, beta, norm_weight, shift, scale, eps):
-    return torch.empty_like(x0)
 
 
 # ---------------------------------------------------------------------------

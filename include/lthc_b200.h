@@ -296,26 +296,6 @@ LTHC_API int lthc_final_norm_modulate_bwd(const void* x, const void* norm_weight
                          size_t workspace_bytes, int64_t B, int64_t T, int64_t C, float eps,
                          int act_dtype, void* stream);
 
-/* ============ materialisation fused with the final norm + modulate =========== */
-/* Inference form of the model's last two steps,
- *   X_L = x0 + sum_l beta_l (.) dz_l            final_accumulate_reference
- *                                               (local_thc.py:1368-1372, 1416-1420)
- *   m   = modulate(RMSNorm(X_L), shift, scale)  FinalLayerSharedAdaLN.forward without
- *                                               its Linear (local_thc.py:865-873)
- * in one pass: X_L is rounded to the activation dtype on chip (as the unfused
- * path stores it) and only m [B, 4G, 4G, C] is written.  norm_weight [C] (16-byte
- * aligned), shift / scale: B rows of C in the activation dtype, row stride
- * mod_stride elements.  C <= 1024.  Runs as thread-block clusters of ceil(C/64)
- * CTAs; lthc_materialise_final_supported() sets *clusters to the number of such
- * clusters the current device can hold at once (0: none fits, and the entry point
- * returns LTHC_ERR_LAUNCH). */
-LTHC_API int lthc_materialise_final_fwd(const void* x0, const void* const* dz, const void* const* beta,
-                                        int beta_dtype, int n_layers, const void* norm_weight,
-                                        int norm_weight_dtype, const void* shift, const void* scale,
-                                        int64_t mod_stride, float eps, void* m_out, int64_t B, int64_t G, int64_t C,
-                                        int act_dtype, void* stream);
-LTHC_API int lthc_materialise_final_supported(int64_t C, int n_layers, int act_dtype, int* clusters);
-
 #ifdef __cplusplus
 }
 #endif

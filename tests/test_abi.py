@@ -66,19 +66,6 @@ P = 256  # a 16-byte aligned non-null address that is never dereferenced
                                       1, None), 1),
     (lambda L: L.lthc_branch_lazy_bwd(P, P, P, P, P, 4612, P, 0, P, 0, P, P, P, P, P, P, 1 << 30, 2, 256, 768, 1,
                                       None), 2),
-    (lambda L: L.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 0, P, P,
-                                            1032, 1e-6, P, 1, 16, 1032, 1, None), 2),
-    (lambda L: L.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 0, P, P,
-                                            700, 1e-6, P, 1, 16, 768, 1, None), 2),
-    (lambda L: L.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 0, P, P,
-                                            1536, -1.0, P, 1, 16, 768, 1, None), 2),
-    (lambda L: L.lthc_materialise_final_fwd(None, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 0, P,
-                                            P, 1536, 1e-6, P, 1, 16, 768, 1, None), 1),
-    (lambda L: L.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P + 4, 0, P,
-                                            P, 1536, 1e-6, P, 1, 16, 768, 1, None), 4),
-    (lambda L: L.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 5, P, P,
-                                            1536, 1e-6, P, 1, 16, 768, 1, None), 3),
-    (lambda L: L.lthc_materialise_final_supported(1032, 12, 1, ctypes.byref(ctypes.c_int())), 2),
 ])
 def test_validation_errors(call, status):
     lib = _lib.load()
@@ -97,8 +84,6 @@ def test_empty_batch_is_a_successful_no_op():
     assert lib.lthc_final_norm_modulate_bwd(P, P, 0, P, 1536, P, P, None, None, None, None, 0, 0, 4096, 768, 1e-6, 1,
                                             None) == 0
     assert lib.lthc_branch_lazy_fwd(P, P, P, P, 4608, P, 0, P, 0, P, P, 0, 256, 768, 1, None) == 0
-    assert lib.lthc_materialise_final_fwd(P, _lib.ptr_array([P] * 12), _lib.ptr_array([P] * 12), 0, 12, P, 0, P, P,
-                                          1536, 1e-6, P, 0, 16, 768, 1, None) == 0
     assert lib.lthc_branch_lazy_bwd(None, P, P, P, P, 4608, P, 0, P, 0, P, P, None, None, None, None, 0, 2, 0, 768, 1,
                                     None) == 0
 

@@ -97,30 +97,3 @@ def test_call_routes_meta_and_cpu_tensors_through_the_dispatcher():
     wc = torch.zeros(768, 16, dtype=torch.bfloat16)
     with pytest.raises((ValueError, NotImplementedError)):
         ops.call(ops.lazy_update, c, c, wc, wc)
-
-
-def test_fused_final_betas_per_model_class_and_default_off():
-    """The betas the fused materialise + final path would pass are the ones each
-    class's installed final_accumulate_reference passes (the write weights uncast
-    for the stacked / released ops, cast to the update dtype for the pure-torch
-    loop); the fused path is off unless FUSE_FINAL is set, and a CPU residual is
-    never offered to it."""
-    L = import_reference()
-    assert integration.FUSE_FINAL is False
-    assert not ops.materialise_final_supported(torch.zeros(1, 16, 16, 64), 12)
-    with integration.install(L):
-        for cls, cast in ((L.SharedReadFusedFinal12LocalTHCSharedAdaLNJiT, False),
-                          (L.SharedReadFusedFinalLocalTHCSharedAdaLNJiT, False),
-                          (L.SharedReadLocalTHCSharedAdaLNJiT, True)):
-            m = cls(depth=12)
-            with torch.no_grad():
-                for i, b in enumerate(m.blocks):
-                    b.write.write_weight.copy_(torch.full_like(b.write.write_weight, 0.1 * (i + 1)))
-            x0 = torch.zeros(1, 64, 64, 768, dtype=torch.bfloat16)
-            updates = [torch.zeros(1, 256, 768, dtype=torch.bfloat16) for _ in range(12)]
-            betas = integration._accumulate_betas(m, x0, updates)
-            assert betas is not None and len(betas) == 12
-            for i, (bt, blk) in enumerate(zip(betas, m.blocks)):
-                assert bt.dtype == (torch.bfloat16 if cast else torch.float32)
-                assert torch.equal(bt, blk.write.write_weight.to(bt.dtype))
-            assert integration._accumulate_betas(m, x0, updates[:11]) is None  # one update per block
