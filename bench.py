@@ -60,6 +60,9 @@ def parse_args():
                    help="skip the LTHC-B/4 images/sec legs (forward, training step, sampling)")
     p.add_argument("--reference-gpu", action="store_true",
                    help="also time the reference's own model on the GPU (needs the reference package)")
+    p.add_argument("--placement-sweep", action="store_true",
+                   help="instead of the benchmark: the materialisation's GB/s over output / x0 placements "
+                        "(swept forward and in reverse) and the per-launch times after an idle GPU")
     return p.parse_args()
 
 
@@ -484,6 +487,63 @@ def _reference_model(dev):
     return fill_seeded_(ref_build("lthc_b4_velocity"), 1).to(dev)
 
 
+# ------------------------------------------------------------------ placement sweep
+def placement_sweep(dev) -> dict:
+    """GB/s of the B = 64 materialisation with its output placed
+    at 0..8 MB (256 KB steps) inside one buffer and x0 at 0..1 MB (64 KB steps),
+    every other buffer fixed; each sweep runs in increasing and then decreasing
+    order, so a drift over time (GPU warming up) and a dependence on placement can
+    be told apart.  Then the per-launch GB/s of 400 back-to-back launches after the
+    GPU idled for 1 s, 0.3 s and not at all."""
+    from flowmatching_lthc_b200 import _lib
+
+    cfg = W.config2(B=B_DEFAULT, device=dev, seed=1)
+    dz, P = cfg["dz"], cfg["P"]
+    nbytes = cfg["x0"].numel() * 2
+    MB = 1 << 20
+    big_out = torch.empty(nbytes + 9 * MB, dtype=torch.uint8, device=dev)
+    big_x = torch.zeros(nbytes + 9 * MB, dtype=torch.uint8, device=dev)
+    big_x[:nbytes].view(torch.bfloat16).copy_(cfg["x0"].reshape(-1))
+    dzp, bp = _lib.ptr_array([t.data_ptr() for t in dz]), _lib.ptr_array([w.data_ptr() for w in P])
+    stream = torch.cuda.current_stream(dev)
+    nb = W.materialise_bytes(B_DEFAULT, G, C, L, 2)
+
+    def run(xp, op):
+        _lib.call("lthc_materialise_fwd", xp, dzp, bp, _lib.DTYPE_F32, L, op, B_DEFAULT, G, C, _lib.DTYPE_BF16,
+                  stream.cuda_stream)
+
+    def gbs(xp, op, it=30):
+        for _ in range(5):
+            run(xp, op)
+        return round(nb / time_device(lambda: run(xp, op), it, stream) / 1e6, 1)
+
+    out: dict = {}
+    for name, offsets, fixed in (("out_offset_kb", range(0, 33), "x"), ("x0_offset_kb", range(0, 17), "out")):
+        step = 256 * 1024 if fixed == "x" else 64 * 1024
+        for order in ("increasing", "decreasing"):
+            ks = list(offsets) if order == "increasing" else list(reversed(offsets))
+            res = {}
+            for k in ks:
+                off = k * step
+                res[off // 1024] = (gbs(big_x.data_ptr(), big_out.data_ptr() + off) if fixed == "x"
+                                    else gbs(big_x.data_ptr() + off, big_out.data_ptr()))
+            out[f"{name}_{order}"] = res
+    for idle in (1.0, 0.3, 0.0):
+        torch.cuda.synchronize()
+        time.sleep(idle)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(401)]
+        ev[0].record(stream)
+        for i in range(400):
+            run(big_x.data_ptr(), big_out.data_ptr())
+            ev[i + 1].record(stream)
+        ev[-1].synchronize()
+        t = [ev[i].elapsed_time(ev[i + 1]) for i in range(400)]
+        out[f"after_idle_{idle}s"] = {"first_5_launches_gbs": [round(nb / x / 1e6) for x in t[:5]],
+                                      "launches_0_20_gbs": round(nb / (sum(t[:20]) / 20) / 1e6),
+                                      "launches_20_400_gbs": round(nb / (sum(t[20:]) / 380) / 1e6)}
+    return out
+
+
 # ------------------------------------------------------------------ reference arm
 def reference_arm(args, r: D.Rank) -> int:
     if not r.is_main:
@@ -584,6 +644,13 @@ def main() -> int:
         D.barrier()
     stream = torch.cuda.current_stream(dev)
     B = args.batch
+    if args.placement_sweep:
+        if r.is_main:
+            print(json.dumps({"placement_sweep": placement_sweep(dev), "kernel": "broadcast_tma_kernel<bf16, 12, base>",
+                              "workload": WORKLOADS["materialise_fwd"]}), flush=True)
+        D.barrier()
+        D.shutdown()
+        return 0
 
     cfg = _op_inputs(B, dev, seed=1000 + r.rank)
     step, bytes_step, launches, kernel = op_step(args.op, cfg)
