@@ -15,6 +15,7 @@ and gradients only.  Reference code used (paths inside the reference repository)
       X_0 + sum_l P_l(dz_l))
   sample_heun / cfg_velocity (two-call CFG)                      flowmatching_lthc/sampling.py:15-53
   build_model("lthc_b4_velocity") state-dict names and shapes    flowmatching_lthc/models/__init__.py:17-28
+  the released LTHC-B/4 size (model_b4): inputs regenerated from the seed, outputs sampled
 """
 from __future__ import annotations
 
@@ -50,6 +51,10 @@ CASES = {
     "model_wide": (dict(input_size=128, patch_size=4, hidden_size=256, depth=12, num_heads=4, bottleneck_dim=128,
                         workspace_grid=8, num_classes=10), 2, 5, 6),
 }
+# The released LTHC-B/4 itself (91.6 M parameters) at B = 2: outputs only, a fixed 1-in-7 sample of them.
+B4_CASE = ("model_b4", dict(input_size=256, patch_size=4, hidden_size=768, depth=12, num_heads=12, bottleneck_dim=128,
+                            workspace_grid=16, num_classes=1000), 2, 7, 8)
+B4_SAMPLE_STRIDE = 7
 # gradients kept for every case (small tensors) and, in the small case only, the larger ones
 GRAD_PARAMS = ("shared_read.read_logits", "blocks.0.write.write_weight", "blocks.11.write.write_weight",
                "final_layer.linear.weight", "final_layer.norm_final.weight", "x_embedder.proj1.weight")
@@ -124,6 +129,27 @@ def make(name: str) -> dict:
     return out
 
 
+def make_b4() -> dict:
+    name, kw, B, wseed, iseed = B4_CASE
+    m = reference_model(kw, wseed)
+    gen = torch.Generator().manual_seed(iseed)
+    x = torch.randn(B, 3, 256, 256, generator=gen)
+    t = torch.rand(B, generator=gen)
+    y = torch.tensor([207, kw["num_classes"]])  # a class and the CFG null label
+    idx = torch.arange(0, B * 3 * 256 * 256, B4_SAMPLE_STRIDE)
+    with torch.no_grad():
+        lazy = m(x, t, y, use_lazy=True)
+        naive = m(x, t, y, use_lazy=False)
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            lazy_bf16 = m(x, t, y, use_lazy=True).float()
+    return {"meta": {"name": name, "kwargs": kw, "batch": B, "weight_seed": wseed, "input_seed": iseed,
+                     "sample_stride": B4_SAMPLE_STRIDE},
+            "t": t, "y": y, "out_lazy_sample": lazy.reshape(-1)[idx].clone(),
+            "out_naive_sample": naive.reshape(-1)[idx].clone(),
+            "out_lazy_bf16_cpu_sample": lazy_bf16.reshape(-1)[idx].clone(),
+            "x_sum": x.double().sum().item()}
+
+
 def b4_keys() -> dict:
     sd = ref_build_model("lthc_b4_velocity").state_dict()
     return {k: list(v.shape) for k, v in sd.items()}
@@ -136,6 +162,10 @@ def main() -> None:
         path = HERE / f"{name}.pt"
         torch.save(case, path)
         print(f"wrote {path} ({path.stat().st_size} bytes)")
+    case = make_b4()
+    path = HERE / f"{case['meta']['name']}.pt"
+    torch.save(case, path)
+    print(f"wrote {path} ({path.stat().st_size} bytes)")
     path = HERE / "b4_state_dict_keys.json"
     path.write_text(json.dumps(b4_keys(), indent=0) + "\n")
     print(f"wrote {path}")

@@ -188,3 +188,29 @@ def test_graphed_sampler_bf16_equals_eager_bf16():
     assert rel(out, eager) < 1e-2
     with pytest.raises(ValueError, match="captured for 2 images"):
         graphed(labels[:1], noise[:1])
+
+
+def test_released_b4_size_matches_the_reference():
+    """The released LTHC-B/4 (91.6 M parameters, 64x64x768 residual, 16x16 workspace)
+    at B = 2: fp32 lazy and naive outputs within 1e-4 of the reference's own (a fixed
+    1-in-7 sample of the output), bf16 autocast within 1.5x the reference's own bf16
+    deviation, on the path with every fused kernel."""
+    g = torch.load(GOLDEN / "model_b4.pt")
+    meta = g["meta"]
+    gen = torch.Generator().manual_seed(meta["input_seed"])
+    x = torch.randn(meta["batch"], 3, 256, 256, generator=gen)
+    assert abs(x.double().sum().item() - g["x_sum"]) < 1e-6 * x.numel()  # same inputs as the fixture
+    m = M.fill_seeded_(M.build_model("lthc_b4_velocity"), meta["weight_seed"]).cuda().eval()
+    xd, t, y = x.cuda(), g["t"].cuda(), g["y"].cuda()
+    stride = meta["sample_stride"]
+    with torch.no_grad():
+        lazy = m(xd, t, y).reshape(-1)[::stride]
+        naive = m(xd, t, y, use_lazy=False).reshape(-1)[::stride]
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            bf = m(xd, t, y).float().reshape(-1)[::stride]
+    gold = g["out_lazy_sample"]
+    assert rel(lazy, gold) < FP32_TOL
+    assert rel(naive, g["out_naive_sample"]) < FP32_TOL
+    ref_bf16 = g["out_lazy_bf16_cpu_sample"]
+    assert rel(bf, gold) < max(1.5 * rel(ref_bf16, gold), 1e-2)
+    assert rms_rel(bf, gold) < max(1.5 * rms_rel(ref_bf16, gold), 1e-2)
