@@ -239,25 +239,6 @@ int encode_workspace_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t 
   return LTHC_OK;
 }
 
-// Workspace [B*G*G, C] as a 3-D map over (channel, cell column, cell row): a box of
-// 64 channels x kStripCells cells of one cell row, so a store of a ragged last strip
-// is clipped at the grid edge instead of spilling into the next cell row.
-template <typename T>
-int encode_cell_rows_map(CUtensorMap* m, const void* ptr, int64_t B, int64_t G, int64_t C) {
-  auto enc = tmap_encoder();
-  if (!enc) return fail(LTHC_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t es = sizeof(T);
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(G), static_cast<cuuint64_t>(B * G)};
-  const cuuint64_t strides[2] = {C * es, G * C * es};
-  const cuuint32_t box[3] = {kSliceCh, kStripCells, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, tmap_dtype<T>(), 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, kL2Promotion,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (cell rows) failed with %d", (int)r);
-  return LTHC_OK;
-}
-
 // Per-device, per-kernel, per-launch-shape set-up (cached): opt in to the dynamic
 // shared memory the launch needs (the attribute only ever grows, so launches of
 // the same kernel with other shapes stay valid) and record how many CTAs of that
@@ -393,7 +374,7 @@ int read_family_t(const ReadJob& j, int sms, cudaStream_t s) {
   for (int l = 0; l < j.L; ++l) {
     if (pool) {
       p.w[l] = j.w[l];
-      LTHC_TRY(encode_cell_rows_map<T>(&p.tm_out[l], j.out[l], j.B, j.G, j.C));
+      p.out[l] = j.out[l];
     }
     if (wgrad) LTHC_TRY(encode_workspace_map<T>(&p.tm_low[l], j.low[l], j.B * j.G * j.G, j.C));
   }

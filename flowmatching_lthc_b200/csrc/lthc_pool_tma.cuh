@@ -12,9 +12,7 @@
 //   next POOL_WARPS warps   POOL: each owns CELLS_PER_POOL cells of the strip and
 //                           reads the weights from a shared-memory copy laid out
 //                           [r][layer pair][lane] as float4 (one 16-byte load
-//                           feeds two layers, conflict-free); the pooled values go
-//                           to a shared-memory output tile that one elected thread
-//                           writes out with a TMA tile store per layer
+//                           feeds two layers, conflict-free)
 //   last warp               producer (one elected lane issues the TMA loads)
 // A strip is kStripCells horizontally adjacent cells; stages hold the H tile
 // [4 rows][4*kStripCells columns][64 channels] and, for WGRAD, the L low tiles
@@ -94,15 +92,8 @@ struct PoolLayout {
   static constexpr int kStages = sizeof(T) == 2 ? kStages16 : (kStages16 + 1) / 2;
   static constexpr int kLayerPairs = (LMAX + 1) / 2;
   static constexpr int kWBytes = POOL ? kPos * kLayerPairs * 32 * 16 : 0;  // [r][lp][lane] float4
-  // Pooled outputs of a strip, [layer][cell][64 channels], written out by TMA tile stores;
-  // two tiles (one for fp32, whose stages are twice as large) so a strip's stores can
-  // still be reading while the next strip is pooled.
-  static constexpr int kOutTileBytes = LMAX * kStripCells * kSliceCh * static_cast<int>(sizeof(T));
-  static constexpr int kOutBufs = sizeof(T) == 4 ? 1 : 2;
-  static constexpr int kOutBytes = POOL ? kOutBufs * kOutTileBytes : 0;
   static constexpr int kWOffset = kStages * kStageBytes;
-  static constexpr int kOutOffset = kWOffset + kWBytes;
-  static constexpr int kBarrierOffset = kOutOffset + kOutBytes;
+  static constexpr int kBarrierOffset = kWOffset + kWBytes;
   static constexpr int kSmemBytes = kBarrierOffset + 2 * kStages * 8 + 128;
   static_assert(kSmemBytes <= 227 * 1024, "read-family stages exceed the shared memory of a CTA");
 };
@@ -110,8 +101,8 @@ struct PoolLayout {
 struct PoolTmaParams {
   CUtensorMap tm_h;                  // 4D (C, 4G, 4G, B) box (64, 16, 4, 1)
   CUtensorMap tm_low[kMaxLayers];    // 2D (C, B*G*G) box (64, 4)        (WGRAD)
-  CUtensorMap tm_out[kMaxLayers];    // 3D (C, G, B*G) box (64, 4, 1) of each T[B, G*G, C] output (POOL)
   const void* w[kMaxLayers];         // [C, 16] weights, dtype w_dtype   (POOL)
+  void* out[kMaxLayers];             // T[B, G*G, C]                     (POOL)
   float* partial;                    // [gridDim.x][L][C][16]            (WGRAD)
   int w_dtype;
   int L;
@@ -290,18 +281,18 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
   if constexpr (POOL) {
     // ---------------- pooling consumers (CELLS_PER_POOL cells x one layer group) ----
     constexpr int GP = Lay::kGroupPairs;
-    constexpr int kPoolThreads = 32 * Lay::kPoolWarps;
     const int pw = warp - kPoolWarp0;
     const int k0 = (pw / Lay::kLayerGroups) * CELLS_PER_POOL;
     const int lp0 = (pw % Lay::kLayerGroups) * GP;  // first layer pair of this warp
     const uint32_t wbase = smem_base + Lay::kWOffset + lane * 16;
-    const bool storer = pw == 0 && lane == 0;       // issues the output tile stores
+    const int64_t GG = static_cast<int64_t>(p.G) * p.G;
     StripCursor cur(s_begin, p.G, p.strips_per_row);
     for (int it = 0; it < n_it; ++it, cur.next()) {
       const int s = it % Lay::kStages;
       if (!mbar_wait(&full[s], (it / Lay::kStages) & 1)) break;
       const int64_t b = cur.b;
       const int wy = cur.wy, wx0 = cur.wx0();
+      const int ncell = min(kStripCells, p.G - wx0);
       const uint32_t sb = smem_base + s * Lay::kStageBytes;
       float2 acc[2 * GP][CELLS_PER_POOL];
 #pragma unroll
@@ -328,32 +319,20 @@ __global__ void __launch_bounds__(PoolLayout<T, (LT > 0 ? LT : kMaxLayers), POOL
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      // Output tile it % kOutBufs: the stores issued from it kOutBufs strips ago must
-      // have read it before it is overwritten.
-      const uint32_t ob = smem_base + Lay::kOutOffset + (it % Lay::kOutBufs) * Lay::kOutTileBytes;
-      if (storer) bulk_wait_read<Lay::kOutBufs - 1>();
-      named_barrier(1, kPoolThreads);
+      if (cvalid) {
+        const int64_t m0 = b * GG + static_cast<int64_t>(wy) * p.G + wx0;
 #pragma unroll
-      for (int k = 0; k < CELLS_PER_POOL; ++k) {
+        for (int k = 0; k < CELLS_PER_POOL; ++k) {
+          if (k0 + k < ncell) {
 #pragma unroll
-        for (int j = 0; j < 2 * GP; ++j) {
-          const int l = 2 * lp0 + j;
-          if (l < L) sts_pair<T>(ob + ((l * kStripCells + k0 + k) * kSliceCh + 2 * lane) * kEs, acc[j][k]);
+            for (int j = 0; j < 2 * GP; ++j) {
+              const int l = 2 * lp0 + j;
+              if (l < L) Act<T>::st(static_cast<T*>(p.out[l]) + (m0 + k0 + k) * p.C + c, acc[j][k]);
+            }
+          }
         }
       }
-      fence_proxy_async_smem();
-      named_barrier(1, kPoolThreads);
-      if (storer) {
-        // Cells past the grid edge (a ragged last strip) and channels past C are
-        // clipped by the 3-D maps.
-        const int32_t rr = static_cast<int32_t>(b * p.G + wy);
-        for (int l = 0; l < L; ++l)
-          tma_store_3d(&p.tm_out[l], smem + (ob - smem_base) + l * kStripCells * kSliceCh * kEs,
-                       static_cast<int32_t>(c0), wx0, rr);
-        bulk_commit();
-      }
     }
-    if (storer) bulk_wait_all();
   }
 }
 
