@@ -409,7 +409,8 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
         if net0 is None:
             continue
         net0.train()
-        net = torch.nn.parallel.DistributedDataParallel(net0, device_ids=[r.local_rank]) if r.world > 1 else net0
+        net = (torch.nn.parallel.DistributedDataParallel(net0, device_ids=[r.local_rank], gradient_as_bucket_view=True)
+               if r.world > 1 else net0)
         opt = torch.optim.AdamW(net0.parameters(), lr=1e-4, fused=True)
 
         def train(net=net, opt=opt):
@@ -422,6 +423,17 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
             train()
         ms = _timed(train, 10, stream)
         leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
+        if tag == "ours" and r.world > 1:
+            # what the gradient exchange costs: the same step with no DDP wrapper (every
+            # rank updates its own copy), and one NCCL all-reduce of the gradient bytes
+            for _ in range(2):
+                train(net0)
+            leg[tag]["ms_per_step_without_exchange"] = round(_timed(lambda: train(net0), 10, stream) / 10, 3)
+            flat = torch.zeros(sum(q.numel() for q in net0.parameters()), device=dev)
+            D.reduce_sum_(flat)
+            leg[tag]["allreduce_ms"] = round(_timed(lambda: D.reduce_sum_(flat), 5, stream) / 5, 3)
+            leg[tag]["allreduce_bytes"] = flat.numel() * 4
+            del flat
         del net, opt
     out["train_step"] = {"config": "BASELINE config 4: fwd+bwd+AdamW, 32 images per GPU, bf16 autocast" +
                          (f", DDP over {r.world} GPUs" if r.world > 1 else ""), "batch_per_gpu": B, "steps": 10,
