@@ -424,11 +424,14 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
         ms = _timed(train, 10, stream)
         leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
         if tag == "ours" and r.world > 1:
-            # what the gradient exchange costs: the same step with no DDP wrapper (every
-            # rank updates its own copy), and one NCCL all-reduce of the gradient bytes
+            # what the gradient exchange costs: the same step under no_sync (every rank
+            # updates its own copy), and one NCCL all-reduce of the gradient bytes
+            def train_local(net=net, train=train):
+                with net.no_sync():  # forward and backward through DDP, gradients not exchanged
+                    train()
             for _ in range(2):
-                train(net0)
-            leg[tag]["ms_per_step_without_exchange"] = round(_timed(lambda: train(net0), 10, stream) / 10, 3)
+                train_local()
+            leg[tag]["ms_per_step_without_exchange"] = round(_timed(train_local, 10, stream) / 10, 3)
             flat = torch.zeros(sum(q.numel() for q in net0.parameters()), device=dev)
             D.reduce_sum_(flat)
             leg[tag]["allreduce_ms"] = round(_timed(lambda: D.reduce_sum_(flat), 5, stream) / 5, 3)
