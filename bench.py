@@ -357,8 +357,10 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
     """Images/sec of the LTHC-B/4 model at N GPUs (whole-job aggregates, device time,
     max over ranks), bf16 autocast, seeded synthetic inputs:
       forward   BASELINE config 3: B = 64 per GPU;
-      train     config 4: fwd + bwd + fused AdamW, 32 images per GPU, DDP (NCCL
-                all-reduce of every gradient) for N > 1;
+      train     config 4: fwd + bwd + fused AdamW, 32 images per GPU; for N > 1 the
+                gradients accumulate into one flat buffer averaged by a single NCCL
+                all-reduce per step (dist.FlatGradients), with the step without any
+                exchange, a bare all-reduce and PyTorch's DDP reported beside it;
       sample    config 5: Heun-50 CFG 1.5 (velocity target) of 1024 images, host-seeded
                 per-image noise and labels sharded over the ranks, doubled batch,
                 each chunk of <= 512 images one captured CUDA graph.
@@ -405,41 +407,51 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
     zt = tt * x1 + (1 - tt) * e
     v = (x1 - zt) / (1 - tt).clamp_min(0.05)
     leg = {}
-    for tag, net0 in (("ours", m), ("reference", refm)):
-        if net0 is None:
-            continue
-        net0.train()
-        net = (torch.nn.parallel.DistributedDataParallel(net0, device_ids=[r.local_rank], gradient_as_bucket_view=True)
-               if r.world > 1 else net0)
-        opt = torch.optim.AdamW(net0.parameters(), lr=1e-4, fused=True)
 
-        def train(net=net, opt=opt):
-            opt.zero_grad(set_to_none=True)
+    def make_step(net, opt, zero, exchange):
+        def train():
+            zero()
             with torch.autocast("cuda", dtype=torch.bfloat16):
                 loss = (v - net(zt, t, y)).float().square().mean()
             loss.backward()
+            exchange()
             opt.step()
+        return train
+
+    def timed_train(step):
         for _ in range(3):
-            train()
-        ms = _timed(train, 10, stream)
-        leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
-        if tag == "ours" and r.world > 1:
-            # what the gradient exchange costs: the same step under no_sync (every rank
-            # updates its own copy), and one NCCL all-reduce of the gradient bytes
-            def train_local(net=net, train=train):
-                with net.no_sync():  # forward and backward through DDP, gradients not exchanged
-                    train()
-            for _ in range(2):
-                train_local()
-            leg[tag]["ms_per_step_without_exchange"] = round(_timed(train_local, 10, stream) / 10, 3)
-            flat = torch.zeros(sum(q.numel() for q in net0.parameters()), device=dev)
-            D.reduce_sum_(flat)
-            leg[tag]["allreduce_ms"] = round(_timed(lambda: D.reduce_sum_(flat), 5, stream) / 5, 3)
-            leg[tag]["allreduce_bytes"] = flat.numel() * 4
-            del flat
+            step()
+        ms = _timed(step, 10, stream)
+        return {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
+
+    # ours: gradients accumulate into one flat buffer, one all-reduce (mean) per step
+    m.train()
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True)
+    fg = D.FlatGradients(m.parameters())
+    leg["ours"] = timed_train(make_step(m, opt, fg.zero_grad, fg.allreduce))
+    if r.world > 1:
+        # the same step without any exchange, one bare all-reduce of the gradient bytes,
+        # and PyTorch's DistributedDataParallel (bucketed all-reduces during backward)
+        leg["ours"]["ms_per_step_without_exchange"] = timed_train(make_step(m, opt, fg.zero_grad, lambda: None))[
+            "ms_per_step"]
+        fg.allreduce()
+        leg["ours"]["allreduce_ms"] = round(_timed(fg.allreduce, 5, stream) / 5, 3)
+        leg["ours"]["allreduce_bytes"] = fg.flat.numel() * 4
+        ddp = torch.nn.parallel.DistributedDataParallel(m, device_ids=[r.local_rank], gradient_as_bucket_view=True)
+        opt_d = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True)
+        leg["ours"]["ddp"] = timed_train(make_step(ddp, opt_d, lambda: opt_d.zero_grad(set_to_none=True),
+                                                   lambda: None))
+        del ddp, opt_d
+    del fg, opt
+    if refm is not None:
+        refm.train()
+        net = (torch.nn.parallel.DistributedDataParallel(refm, device_ids=[r.local_rank]) if r.world > 1 else refm)
+        opt = torch.optim.AdamW(refm.parameters(), lr=1e-4, fused=True)
+        leg["reference"] = timed_train(make_step(net, opt, lambda: opt.zero_grad(set_to_none=True), lambda: None))
         del net, opt
     out["train_step"] = {"config": "BASELINE config 4: fwd+bwd+AdamW, 32 images per GPU, bf16 autocast" +
-                         (f", DDP over {r.world} GPUs" if r.world > 1 else ""), "batch_per_gpu": B, "steps": 10,
+                         (f", data-parallel over {r.world} GPUs (one all-reduce of the flat gradient per step)"
+                          if r.world > 1 else ""), "batch_per_gpu": B, "steps": 10,
                          **leg.pop("ours"), **({"reference_gpu": leg["reference"]} if leg else {})}
     # the training step changed the weights: sample with fresh ones
     m = _model(dev)

@@ -65,6 +65,41 @@ def reduce_sum_(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+class FlatGradients:
+    """Data-parallel gradient exchange as one collective per step.
+
+    Every trainable parameter's ``.grad`` is made a view into one contiguous fp32
+    buffer, so backward accumulates straight into it; ``allreduce()`` then averages
+    the whole buffer over the ranks with a single all-reduce (a no-op on one rank).
+    The result equals DistributedDataParallel's (the mean of the per-rank
+    gradients); the exchange is one large collective after backward instead of
+    DDP's bucketed collectives interleaved with it, which on one NVSwitch node
+    cost more than the transfer itself.  Call ``zero_grad()`` instead of the
+    optimiser's (the views must survive; ``set_to_none`` would drop them)."""
+
+    def __init__(self, params) -> None:
+        self.params = [q for q in params if q.requires_grad]
+        if not self.params:
+            raise ValueError("no trainable parameters")
+        dev = self.params[0].device
+        if any(q.dtype != torch.float32 or q.device != dev for q in self.params):
+            raise ValueError("FlatGradients expects fp32 parameters on one device")
+        self.flat = torch.zeros(sum(q.numel() for q in self.params), device=dev)
+        off = 0
+        for q in self.params:
+            q.grad = self.flat[off:off + q.numel()].view_as(q)
+            off += q.numel()
+
+    def zero_grad(self) -> None:
+        self.flat.zero_()
+
+    def allreduce(self) -> None:
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(self.flat, op=dist.ReduceOp.AVG if self.flat.is_cuda else dist.ReduceOp.SUM)
+            if not self.flat.is_cuda:  # gloo has no AVG
+                self.flat.div_(dist.get_world_size())
+
+
 def barrier() -> None:
     if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
         dist.barrier()

@@ -73,3 +73,52 @@ def test_gloo_two_ranks_weight_grad_allreduce_and_max():
     err, scale, slowest = q.get(timeout=5)
     assert err <= 1e-6 * scale
     assert slowest == 2.0
+
+
+def _flat_worker(rank: int, world: int, port: int, q) -> None:
+    """A small model's data-parallel step with FlatGradients: after the one
+    all-reduce every rank holds the full-batch mean gradient, which equals what a
+    single process computes on the whole batch (the loss is a mean over images)."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(1)
+    D.init("gloo", D.Rank(rank, world, rank), timeout_s=60)
+    try:
+        torch.manual_seed(0)
+        net = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.SiLU(), torch.nn.Linear(16, 4))
+        x = torch.randn(6, 8, generator=torch.Generator().manual_seed(1))
+        y = torch.randn(6, 4, generator=torch.Generator().manual_seed(2))
+        fg = D.FlatGradients(net.parameters())
+        a, b = D.shard(6, rank, world)
+        fg.zero_grad()
+        ((net(x[a:b]) - y[a:b]).square().mean(1).sum() / (b - a)).backward()
+        fg.allreduce()
+        got = torch.cat([q.grad.reshape(-1) for q in net.parameters()])
+        assert got.data_ptr() != 0 and all(q.grad.data_ptr() >= fg.flat.data_ptr() for q in net.parameters())
+        ref = [torch.zeros_like(q) for q in net.parameters()]
+        for i in range(6):  # the full batch on one process: mean over images of the per-image loss
+            g = torch.autograd.grad((net(x[i:i + 1]) - y[i:i + 1]).square().mean(), list(net.parameters()))
+            ref = [r + gi / 6 for r, gi in zip(ref, g)]
+        want = torch.cat([r.reshape(-1) for r in ref])
+        if rank == 0:
+            q.put((got - want).abs().max().item())
+        D.barrier()
+    finally:
+        D.shutdown()
+
+
+def test_gloo_flat_gradient_allreduce_equals_the_full_batch_gradient():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_flat_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) < 1e-6
