@@ -170,25 +170,32 @@ def _(x: Tensor, alpha: Tensor) -> Tensor:
 
 
 @_custom_op("read_bwd")
-def read_bwd(x: Tensor, grad_z: Tensor, alpha: Tensor, need_grad_x: bool, need_grad_alpha: bool) -> tuple[Tensor, Tensor]:
-    """grad_x = alpha (.) grad_z broadcast; grad_alpha = sum x*grad_z (fp32 [C,16])."""
+def read_bwd(x: Tensor, grad_z: Tensor, alpha: Tensor, need_grad_x: bool, need_grad_alpha: bool,
+             grad_x_in: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """grad_x = (grad_x_in +) alpha (.) grad_z broadcast, fp32 accumulation and one
+    rounding; grad_alpha = sum x*grad_z (fp32 [C,16])."""
     _require_cuda(x, grad_z, alpha)
     b, g, c = _hi_geom(x, "read_bwd")
     x, grad_z, alpha = x.contiguous(), grad_z.contiguous(), alpha.contiguous()
+    if grad_x_in is not None:
+        _require_cuda(grad_x_in)
+        if grad_x_in.shape != x.shape:
+            raise ValueError(f"read_bwd: grad_x_in must be {tuple(x.shape)}, got {tuple(grad_x_in.shape)}")
+        grad_x_in = grad_x_in.to(x.dtype).contiguous()
     gx = torch.empty_like(x) if need_grad_x else x.new_empty((0,))
     ga = torch.empty((c, 16), device=x.device, dtype=torch.float32) if need_grad_alpha else x.new_empty((0,),
                                                                                                       dtype=torch.float32)
     with _guard(x):
         ws_bytes = _lib.load().lthc_read_bwd_workspace_bytes(b, g, c) if need_grad_alpha else 0
         ws = _workspace(ws_bytes, x.device) if need_grad_alpha else None
-        _lib.call("lthc_read_bwd", x.data_ptr(), grad_z.data_ptr(), alpha.data_ptr(), _code(alpha, "read_bwd"), None,
-                  gx.data_ptr() if need_grad_x else None, ga.data_ptr() if need_grad_alpha else None, _p(ws), ws_bytes,
+        _lib.call("lthc_read_bwd", x.data_ptr(), grad_z.data_ptr(), alpha.data_ptr(), _code(alpha, "read_bwd"),
+                  _p(grad_x_in) if need_grad_x else None, gx.data_ptr() if need_grad_x else None, ga.data_ptr() if need_grad_alpha else None, _p(ws), ws_bytes,
                   b, g, c, _code(x, "read_bwd"), _stream(x))
     return gx, ga
 
 
 @read_bwd.register_fake
-def _(x, grad_z, alpha, need_grad_x, need_grad_alpha):
+def _(x, grad_z, alpha, need_grad_x, need_grad_alpha, grad_x_in=None):
     c = x.shape[-1]
     gx = torch.empty_like(x) if need_grad_x else x.new_empty((0,))
     ga = x.new_empty((c, 16), dtype=torch.float32) if need_grad_alpha else x.new_empty((0,), dtype=torch.float32)
@@ -751,8 +758,11 @@ def _embed_setup(ctx, inputs, output):
 
 
 def _embed_backward(ctx, g_x0, g_z):
-    """Read backward (lthc_read_bwd) into grad X0, then the two convolutions'
-    backward as library GEMMs on the bf16 operands (h1 recomputed)."""
+    """The read's backward with the gradient X0 already receives from the
+    materialisation as its base: grad X0 = g_x0 + alpha (.) bcast(g_z) in one
+    write-family pass (no separate read-backward output and add), grad alpha from
+    the same call's weight-gradient pass; then the two convolutions' backward as
+    library GEMMs on the bf16 operands (h1 recomputed)."""
     img, w1, w2, alpha, x0 = ctx.saved_tensors
     need_img, need_w1, need_w2, need_b2, need_a = ctx.needs_input_grad
     bf = torch.bfloat16
@@ -761,8 +771,7 @@ def _embed_backward(ctx, g_x0, g_z):
     gx = g_x0 if g_x0 is not None else torch.zeros_like(x0)
     ga = None
     if g_z is not None:
-        gxr, ga = read_bwd(x0, g_z.to(bf), alpha.to(bf), True, need_a)
-        gx = gx.to(bf) + gxr
+        gx, ga = read_bwd(x0, g_z.to(bf), alpha.to(bf), True, need_a, g_x0.to(bf) if g_x0 is not None else None)
     g2 = gx.to(bf).reshape(-1, c)                                              # [tokens, C]
     patches = (img.to(bf).reshape(b, cin, h, 4, h, 4).permute(0, 2, 4, 1, 3, 5).reshape(-1, cin * 16))
     w1b = w1.to(bf).reshape(128, cin * 16)

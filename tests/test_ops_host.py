@@ -27,6 +27,8 @@ def test_fake_shapes():
     assert torch.ops.lthc_b200.write(dz[0], be[0]).shape == (2, 64, 64, 768)
     assert torch.ops.lthc_b200.lazy_update(dz[0], dz[1], be[0], be[1]).shape == (2, 256, 768)
     assert torch.ops.lthc_b200.weight_grad(x, dz[:3]).shape == (3, 768, 16)
+    gx, ga = torch.ops.lthc_b200.read_bwd(x, dz[0], a, True, True, x)
+    assert gx.shape == x.shape and ga.shape == (768, 16)
     gdz = torch.ops.lthc_b200.materialise_grad_dz(x, be)
     assert len(gdz) == 12 and gdz[0].shape == (2, 256, 768)
     assert torch.ops.lthc_b200.materialise_grad_beta(x, dz).shape == (12, 768, 16)

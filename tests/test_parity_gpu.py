@@ -143,6 +143,12 @@ def test_read_backward(dt, B, G, C):
     gx, ga = ops.read_bwd(x.cuda(), gz.cuda(), a.cuda(), True, True)
     assert same_bits(gx, O.write(gz, a))
     assert rel_err(ga, O.weight_grad(x, [gz])[0]) < RTOL_REDUCTION
+    # accumulating onto a gradient X already holds (the patch embedding's backward
+    # passes the materialisation's gradient): base + alpha (.) bcast(grad_z), one rounding
+    base = rnd(B, 4 * G, 4 * G, C, dtype=dt, seed=153)
+    gx2, ga2 = ops.read_bwd(x.cuda(), gz.cuda(), a.cuda(), True, True, base.cuda())
+    assert same_bits(gx2, O.write_add(base, gz, a))
+    assert torch.equal(ga2, ga)
 
 
 @pytest.mark.parametrize("dt", DTYPES)
