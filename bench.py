@@ -276,6 +276,11 @@ def op_step(op: str, cfg: dict):
                             "broadcast_tma_kernel<bf16, 12, base>"),
         "materialise_bwd": (lambda: ops.call(ops.materialise_bwd, g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2), 2,
                             "pool_tma_kernel<bf16, 12, pool, wgrad> + reduce_partials_kernel"),
+        "materialise_grad_dz": (lambda: ops.call(ops.materialise_grad_dz, g, P), W.materialise_grad_dz_bytes(B, G, C, L, 2),
+                                1, "pool_tma_kernel<bf16, 12, pool>"),
+        "materialise_grad_beta": (lambda: ops.call(ops.materialise_grad_beta, g, dz),
+                                  W.materialise_grad_beta_bytes(B, G, C, L, 2), 2,
+                                  "pool_tma_kernel<bf16, 12, wgrad> + reduce_partials_kernel"),
         "read_fwd": (lambda: ops.call(ops.read, x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
         "read_bwd": (lambda: ops.call(ops.read_bwd, x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
                      "broadcast_tma_kernel<bf16, 1> + pool_tma_kernel<bf16, 1, wgrad> + reduce_partials_kernel"),
@@ -322,7 +327,7 @@ def op_step(op: str, cfg: dict):
     return table[op]
 
 
-OPS = ("materialise_fwd", "materialise_bwd", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
+OPS = ("materialise_fwd", "materialise_bwd", "materialise_grad_dz", "materialise_grad_beta", "read_fwd", "read_bwd", "write_add_fwd", "lazy_fwd", "lazy_bwd",
        "final_fwd", "final_bwd", "embed_fwd", "branch_fwd", "branch_bwd")
 
 
@@ -611,6 +616,8 @@ def reference_arm(args, r: D.Rank) -> int:
 WORKLOADS = {
     "materialise_fwd": "materialise fwd X_L = X_0 + sum_l P_l(dZ_l), BASELINE config 2",
     "materialise_bwd": "materialise bwd (grad dZ_l and grad P_l from grad X_L), config 2 shapes",
+    "materialise_grad_dz": "materialise bwd, pooling half alone (grad dZ_l from grad X_L), config 2 shapes",
+    "materialise_grad_beta": "materialise bwd, weight-gradient half alone (grad P_l), config 2 shapes",
     "read_fwd": "shared read Z = R(X_0), config 2 shapes",
     "read_bwd": "read bwd (grad X_0 and grad alpha), config 2 shapes",
     "write_add_fwd": "write_add X + P(dZ), config 2 shapes",

@@ -95,6 +95,16 @@ def materialise_bwd_bytes(B: int, G: int, C: int, L: int, act_bytes: int, w_byte
     return hi * act_bytes + 2 * L * lo * act_bytes + L * C * 16 * (w_bytes + 4)
 
 
+def materialise_grad_dz_bytes(B: int, G: int, C: int, L: int, act_bytes: int, w_bytes: int = 4) -> int:
+    """The backward's pooling half alone: read grad_out and the weights, write the L update grads."""
+    return (B * 16 * G * G * C + L * B * G * G * C) * act_bytes + L * C * 16 * w_bytes
+
+
+def materialise_grad_beta_bytes(B: int, G: int, C: int, L: int, act_bytes: int) -> int:
+    """The backward's weight-gradient half alone: read grad_out and the L updates, write the fp32 weight grads."""
+    return (B * 16 * G * G * C + L * B * G * G * C) * act_bytes + L * C * 16 * 4
+
+
 def read_bytes(B: int, G: int, C: int, act_bytes: int, w_bytes: int) -> int:
     hi = B * 16 * G * G * C
     lo = B * G * G * C
