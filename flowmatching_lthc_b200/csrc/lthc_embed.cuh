@@ -140,9 +140,12 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
   int it = 0;
 
   // Patch gather: 4 pixels (one token, one channel, one kernel row) per load;
-  // load i of this thread covers pixel-row group i * kEmbedThreads + tid.
+  // load i of this thread covers pixel-row group i * kEmbedThreads + tid.  The
+  // loaded words stay raw (fp32 pixels as 16 bytes, bf16 as 8) until they are
+  // stored into A1 a tile later: converting them at load time would make every
+  // thread wait there for its global loads.
   const int per_tile = p.in_ch * 16 * kEmbedTileCols;
-  uint2 pre[kEmbedMaxLoads];  // next tile's pixels as bf16
+  uint4 pre[kEmbedMaxLoads];  // next tile's pixels, as loaded
   auto gather_load = [&](int64_t t) {
     const int64_t bb = t / (cell_rows * halves);
     const int rr = static_cast<int>(t - bb * cell_rows * halves);
@@ -158,17 +161,15 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
         const int64_t gx = 4 * (static_cast<int64_t>(kEmbedTileCols) * hx_ + tx);
         const int64_t off = ((bb * p.in_ch + c) * img_w + gy) * img_w + gx;
         if (p.img_f32) {
-          const float4 v = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(p.img) + off));
-          __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-          pre[j].x = *reinterpret_cast<uint32_t*>(&lo);
-          pre[j].y = *reinterpret_cast<uint32_t*>(&hi);
+          pre[j] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const float*>(p.img) + off));
         } else {
-          pre[j] = __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.img) + off));
+          const uint2 v = __ldcs(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.img) + off));
+          pre[j] = make_uint4(v.x, v.y, 0u, 0u);
         }
       }
     }
   };
-  auto gather_store = [&](const uint2 (&v)[kEmbedMaxLoads]) {
+  auto gather_store = [&](const uint4 (&v)[kEmbedMaxLoads]) {
 #pragma unroll
     for (int j = 0; j < kEmbedMaxLoads; ++j) {
       const int i = j * kEmbedThreads + tid;
@@ -177,7 +178,16 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
         const int py = (i / kEmbedTileCols) % 16;
         const int c = i / (kEmbedTileCols * 16);
         const int mm = 16 * (tx >> 2) + 4 * (py >> 2) + (tx & 3);
-        *reinterpret_cast<uint2*>(smem + EmbedSmem::kA1 + sw128_offset(mm, c * 16 + (py & 3) * 4)) = v[j];
+        uint2 b;
+        if (p.img_f32) {
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(__uint_as_float(v[j].x), __uint_as_float(v[j].y));
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(__uint_as_float(v[j].z), __uint_as_float(v[j].w));
+          b.x = *reinterpret_cast<const uint32_t*>(&lo);
+          b.y = *reinterpret_cast<const uint32_t*>(&hi);
+        } else {
+          b = make_uint2(v[j].x, v[j].y);
+        }
+        *reinterpret_cast<uint2*>(smem + EmbedSmem::kA1 + sw128_offset(mm, c * 16 + (py & 3) * 4)) = b;
       }
     }
   };
