@@ -21,6 +21,11 @@ Every step of the forward that touches the high-resolution residual runs in
   weights passed uncast (``:1416-1420``);
 * the final RMSNorm + shared-AdaLN modulate over the 4096 tokens (``:865-873``).
 
+The same norm + modulate kernel also runs the branch's two AdaLN prologues,
+``modulate(norm1(z), shift_msa, scale_msa)`` and ``modulate(norm2(z + dz_attn),
+...)`` (``:320-322``): one pass over the workspace rows instead of the eager
+chain of casts, reductions and products.
+
 The workspace Transformer between them (RMSNorm, QK-normed attention with 2-D
 RoPE through ``scaled_dot_product_attention``, SwiGLU, AdaLN) is plain PyTorch
 with the reference's arithmetic (``local_thc.py:175-323``,
@@ -68,6 +73,17 @@ class RMSNorm(nn.Module):
 def modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """Shared-AdaLN modulation of token rows by per-image shift / scale (local_thc.py:37-38)."""
     return x * (1 + scale.unsqueeze(1)) + shift.unsqueeze(1)
+
+
+def norm_modulate(norm: RMSNorm, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """modulate(norm(x), shift, scale) over token rows [B, T, C]: one kernel
+    (lthc_final_norm_modulate, the reference's op-by-op rounding) when x, shift and
+    scale share a dtype, else the eager expression.  The shift / scale halves of a
+    chunked AdaLN output are read in place."""
+    if (x.is_cuda and x.dim() == 3 and x.dtype == shift.dtype == scale.dtype and x.shape[-1] % 8 == 0
+            and x.shape[-1] <= ops.FINAL_MAX_CHANNELS):
+        return ops.call(ops.final_norm_modulate, x, norm.weight, shift, scale, norm.eps)
+    return modulate(norm(x), shift, scale)
 
 
 def _rope_tables(half_head_dim: int, grid: int, theta: float = 10000.0) -> tuple[torch.Tensor, torch.Tensor]:
@@ -157,8 +173,8 @@ class WorkspaceBranch(nn.Module):
 
     def parts(self, z: torch.Tensor, t6: torch.Tensor, rope: WorkspaceRope):
         sh_a, sc_a, g_a, sh_m, sc_m, g_m = t6.chunk(6, dim=-1)
-        dz_attn = g_a.unsqueeze(1) * self.attn(modulate(self.norm1(z), sh_a, sc_a), rope)
-        mlp_out = self.mlp(modulate(self.norm2(z + dz_attn), sh_m, sc_m))
+        dz_attn = g_a.unsqueeze(1) * self.attn(norm_modulate(self.norm1, z, sh_a, sc_a), rope)
+        mlp_out = self.mlp(norm_modulate(self.norm2, z + dz_attn, sh_m, sc_m))
         return dz_attn, mlp_out, g_m
 
     def forward(self, z: torch.Tensor, t6: torch.Tensor, rope: WorkspaceRope) -> torch.Tensor:
@@ -264,10 +280,7 @@ class FinalLayer(nn.Module):
 
     def forward(self, x: torch.Tensor, t2: torch.Tensor) -> torch.Tensor:
         shift, scale = t2.chunk(2, dim=1)
-        if x.dtype != shift.dtype:
-            return self.linear(modulate(self.norm_final(x), shift, scale))
-        return self.linear(ops.call(ops.final_norm_modulate, x, self.norm_final.weight, shift, scale,
-                                    self.norm_final.eps))
+        return self.linear(norm_modulate(self.norm_final, x, shift, scale))
 
 
 # ---------------------------------------------------------------------------

@@ -112,7 +112,8 @@ def test_bf16_autocast_forward_within_the_references_own_bf16_error(name):
 def test_bf16_autocast_runs_the_fused_kernels():
     """The wide case has shapes every fused kernel takes: the tensor-core patch
     embedding, the branch epilogue + lazy update, the materialisation and the
-    final norm + modulate are each called (and nothing falls back to eager)."""
+    norm + modulate (final layer and the branches' AdaLN prologues) are each
+    called (and nothing falls back to eager)."""
     g, m = load("model_wide")
     x, t, y = g["x"].cuda(), g["t"].cuda(), g["y"].cuda()
     assert ops.embed_supported(x, m.x_embedder.proj1.weight, m.x_embedder.proj2.weight)
@@ -134,7 +135,8 @@ def test_bf16_autocast_runs_the_fused_kernels():
     finally:
         ops.call = real_call
     assert seen.count("patch_embed_read") == 1 and seen.count("branch_lazy_update") == 12
-    assert seen.count("materialise") == 1 and seen.count("final_norm_modulate") == 1
+    # the final layer's norm + modulate and each block's two AdaLN prologues
+    assert seen.count("materialise") == 1 and seen.count("final_norm_modulate") == 1 + 2 * 12
     assert "lazy_update" not in seen and "read" not in seen
 
 
