@@ -17,7 +17,8 @@ Patched methods (``flowmatching_lthc/models/local_thc.py``):
   SharedReadFusedFinal12LocalTHCSharedAdaLNJiT.final_accumulate_reference :1416-1420 (released op)
   FinalLayerSharedAdaLN.forward (RMSNorm + modulate fused; the Linear stays)   :865-873
   SharedReadLocalTHCSharedAdaLNJiT.forward_lazy (patch embedding + shared read
-      fused on the tensor cores under bf16 autocast; each block's branch
+      fused on the tensor cores under bf16 autocast; each block's two AdaLN
+      prologues, :320-322, on the norm + modulate kernel and its branch
       epilogue, :318-323, fused with its lazy update)                  :1374-1388
 
 Shape checks and messages are the reference's own; the arithmetic runs in
@@ -119,6 +120,17 @@ def _embed_and_read(model, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]
     return ops.call(ops.patch_embed_read, x, emb.proj1.weight, emb.proj2.weight, emb.proj2.bias, alpha)
 
 
+def _norm_modulate(norm, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """modulate(norm(x), shift, scale) (local_thc.py:320-322) as one norm + modulate
+    kernel when norm is the reference's own RMSNorm and x, shift, scale share a
+    dtype; otherwise the reference's expression."""
+    if (_LTHC is not None and type(norm).forward is _LTHC.RMSNorm.forward and x.is_cuda and x.dim() == 3
+            and x.dtype == shift.dtype == scale.dtype and x.shape[-1] % 8 == 0
+            and x.shape[-1] <= ops.FINAL_MAX_CHANNELS):
+        return ops.call(ops.final_norm_modulate, x, norm.weight, shift, scale, norm.eps)
+    return _ORIGINAL_MODULATE(norm(x), shift, scale)
+
+
 def _branch_and_update(block, z: torch.Tensor, t6: torch.Tensor, rope, shared_read) -> tuple[torch.Tensor, torch.Tensor]:
     """dz = block.branch_update(z, t6, rope) and z' = block.lazy_workspace_update(z, dz,
     shared_read), with the branch's output epilogue (gate product and sum,
@@ -132,8 +144,8 @@ def _branch_and_update(block, z: torch.Tensor, t6: torch.Tensor, rope, shared_re
         dz = block.branch_update(z, t6, rope)
         return dz, block.lazy_workspace_update(z, dz, shared_read)
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = t6.chunk(6, dim=-1)
-    dz_attn = gate_msa.unsqueeze(1) * br.attn(_ORIGINAL_MODULATE(br.norm1(z), shift_msa, scale_msa), rope)
-    mlp_out = br.mlp(_ORIGINAL_MODULATE(br.norm2(z + dz_attn), shift_mlp, scale_mlp))
+    dz_attn = gate_msa.unsqueeze(1) * br.attn(_norm_modulate(br.norm1, z, shift_msa, scale_msa), rope)
+    mlp_out = br.mlp(_norm_modulate(br.norm2, z + dz_attn, shift_mlp, scale_mlp))
     if not (z.dtype == dz_attn.dtype == mlp_out.dtype == gate_mlp.dtype):
         dz = dz_attn + gate_mlp.unsqueeze(1) * mlp_out
         return dz, block.lazy_workspace_update(z, dz, shared_read)
