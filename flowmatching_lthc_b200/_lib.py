@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("liblthc_b200.so")
@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_materialise12_fwd": (_I, [_P, _PP, _PP, _I, _P, _L, _L, _L, _I, _P]),
     "lthc_materialise_bwd_workspace_bytes": (c_size_t, [_L, _L, _L, _I]),
     "lthc_materialise_bwd": (_I, [_P, _PP, _PP, _I, _I, _PP, _P, _P, c_size_t, _L, _L, _L, _I, _P]),
+    "lthc_materialise_bwd_uses_tensor_cores": (_I, [_L, _L, _L, _I, _I]),
     "lthc_write_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
     "lthc_write_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, c_size_t, _L, _L, _L, _I, _P]),
     "lthc_read_fwd": (_I, [_P, _P, _I, _P, _L, _L, _L, _I, _P]),
@@ -58,6 +59,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lthc_lazy_update_bwd_workspace_bytes": (c_size_t, [_L, _L]),
     "lthc_lazy_update_bwd": (_I, [_P, _P, _P, _I, _P, _I, _P, _P, _P, _P, c_size_t, _L, _L, _I, _P]),
     "lthc_selftest_umma": (_I, [_P, _P, _P, _I, _I, _P, _P]),
+    "lthc_selftest_umma_desc": (_I, [_P, _I, _P, _I, _P, _P, _I, c_uint32, _I, _P, _P, _P]),
     "lthc_branch_lazy_fwd": (_I, [_P, _P, _P, _P, _L, _P, _I, _P, _I, _P, _P, _L, _L, _L, _I, _P]),
     "lthc_branch_lazy_bwd_workspace_bytes": (c_size_t, [_L, _L, _L]),
     "lthc_branch_lazy_bwd": (_I, [_P, _P, _P, _P, _P, _L, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, c_size_t, _L, _L,

@@ -22,6 +22,7 @@
 #include "lthc_umma.cuh"
 #include "lthc_embed.cuh"
 #include "lthc_branch.cuh"
+#include "lthc_matbwd_tc.cuh"
 
 namespace lthc {
 
@@ -320,6 +321,113 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
     case LTHC_DTYPE_BF16: return broadcast_t<__nv_bfloat16>(base, dz, w, w_dtype, L, out, B, G, C, sms, s);
     default: return broadcast_t<__half>(base, dz, w, w_dtype, L, out, B, G, C, sms, s);
   }
+}
+
+// ---- materialisation backward on the tensor cores ---------------------------------
+
+#ifndef LTHC_MATBWD_TC
+#define LTHC_MATBWD_TC 1  // 0: every materialisation backward runs the CUDA-core read-family kernel
+#endif
+
+// Launch plan of matbwd_tc_kernel; ok = false when the shape or dtype is not one
+// it takes (fp32, a single layer, C not a multiple of 16, a grid side that does
+// not tile into 32-cell stages, or a cell count that is not a whole number of
+// 128-cell tiles): those run the CUDA-core kernel.
+struct MbPlan {
+  bool ok = false;
+  int Gq = 0, Rq = 0, Lp = 0, stages = 0, visits = 0;
+  int64_t S = 0, Tc = 0, parts = 0, grid = 0;
+  size_t smem = 0, ws = 0;
+};
+
+MbPlan mb_plan(int64_t B, int64_t G, int64_t C, int L, int act, int sms) {
+  MbPlan m;
+  if (!LTHC_MATBWD_TC || act == LTHC_DTYPE_F32 || L < 2 || L > kMaxLayers || C % kMbSliceCh || B < 1) return m;
+  if (G < 8 || (G <= 32 ? 32 % G : G % 32)) return m;
+  const int64_t cells = B * G * G;
+  if (cells % kMbTileCells || cells > INT32_MAX) return m;
+  m.Gq = static_cast<int>(std::min<int64_t>(G, 32));
+  m.Rq = 32 / m.Gq;
+  m.Lp = L + (L & 1);
+  const size_t stage = kMbGxBytes + static_cast<size_t>(L) * kMbDzLayerBytes;
+  const size_t fixed = kMbTRegion + kMbBetaBytes + kMbBarriers * 8 + 16 + 1024;  // + alignment slack
+  const size_t budget = 227 * 1024;
+  m.stages = static_cast<int>(std::min<size_t>(kMbMaxStages, (budget - fixed) / stage));
+  if (m.stages < 2) return m;
+  m.smem = fixed + m.stages * stage;
+  m.Tc = cells / kMbTileCells;
+  m.S = C / kMbSliceCh;
+  // parts CTAs per slice (each a contiguous cell range), or one CTA per SM over
+  // several slices when there are more slices than SMs
+  m.parts = std::max<int64_t>(1, std::min<int64_t>(sms / m.S, m.Tc));
+  m.grid = std::min<int64_t>(m.parts * m.S, sms);
+  m.visits = static_cast<int>(ceil_div(m.S, m.grid));
+  m.ws = static_cast<size_t>(m.grid) * m.visits * L * kMbSliceCh * kPos * sizeof(float);
+  m.ok = true;
+  return m;
+}
+
+template <typename T>
+int matbwd_tc_t(const MbPlan& m, const void* grad_out, const void* const* dz, const void* const* beta, int beta_dtype,
+                int L, void* const* grad_dz, float* grad_beta, void* ws, int64_t B, int64_t G, int64_t C,
+                cudaStream_t s) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(LTHC_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  MatBwdTcParams p;
+  memset(&p, 0, sizeof(p));
+  const cuuint64_t es = sizeof(T);
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  {
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(4 * G),
+                                static_cast<cuuint64_t>(4 * G), static_cast<cuuint64_t>(B)};
+    const cuuint64_t strides[3] = {C * es, 4 * G * C * es, 16 * G * G * C * es};
+    const cuuint32_t box[4] = {kMbSliceCh, static_cast<cuuint32_t>(4 * m.Gq), static_cast<cuuint32_t>(4 * m.Rq), 1};
+    CUresult r = enc(&p.tm_gx, tmap_dtype<T>(), 4, const_cast<void*>(grad_out), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, kL2Promotion,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (grad X_L tiles) failed with %d", (int)r);
+  }
+  const bool wgrad = grad_beta != nullptr;
+  bool st256 = true;
+  for (int l = 0; l < L; ++l) {
+    if (wgrad) p.dz[l] = dz[l];
+    if (grad_dz) st256 = st256 && (reinterpret_cast<uintptr_t>(grad_dz[l]) & 31u) == 0;
+  }
+  p.st256 = st256 ? 1 : 0;
+  for (int l = 0; l < L; ++l) {
+    if (grad_dz) {
+      p.beta[l] = beta[l];
+      p.gdz[l] = grad_dz[l];
+    }
+  }
+  p.partial = wgrad ? static_cast<float*>(ws) : nullptr;
+  p.beta_dtype = beta_dtype;
+  p.L = L;
+  p.Lp = m.Lp;
+  p.G = static_cast<int>(G);
+  p.Gq = m.Gq;
+  p.Rq = m.Rq;
+  p.stages = m.stages;
+  p.need_pool = grad_dz != nullptr;
+  p.need_wgrad = wgrad;
+  p.visits = m.visits;
+  p.C = C;
+  p.S = m.S;
+  p.Tc = m.Tc;
+  p.parts = m.parts;
+  int per_sm = 0;
+  LTHC_TRY(resident_ctas(matbwd_tc_kernel<T>, kMbThreads, static_cast<int>(m.smem), &per_sm));
+  if (per_sm < 1) return fail(LTHC_ERR_LAUNCH, "the tensor-core backward does not fit on an SM");
+  matbwd_tc_kernel<T><<<static_cast<unsigned>(m.grid), kMbThreads, m.smem, s>>>(p);
+  LTHC_TRY(launched("materialisation backward (tensor cores)"));
+  if (wgrad) {
+    const int64_t n = static_cast<int64_t>(L) * C * kPos;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, 256), m.grid * 4);
+    matbwd_tc_finalize_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<const float*>(ws), grad_beta,
+                                                                            L, C, m.S, m.parts, m.grid, m.visits);
+    LTHC_TRY(launched("materialisation backward weight-gradient finalize"));
+  }
+  return LTHC_OK;
 }
 
 // ---- materialisation fused with the final norm + modulate (clusters) ----------
@@ -665,6 +773,44 @@ int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int
   return launched("tcgen05 self-test");
 }
 
+int lthc_selftest_umma_desc(const void* a_img, int a_bytes, const void* b_img, int b_bytes, const uint64_t* a_desc,
+                            const uint64_t* b_desc, int steps, uint32_t idesc, int N, float* D, int* status_dev,
+                            void* stream) {
+  if (!a_img || !b_img || !a_desc || !b_desc || !D || !status_dev)
+    return fail(LTHC_ERR_NULL_POINTER, "images, descriptors, D and status must be set");
+  if (!aligned16(a_img) || !aligned16(b_img)) return fail(LTHC_ERR_ALIGNMENT, "operand images must be 16-byte aligned");
+  if (a_bytes < 16 || a_bytes > kUmmaProbeRegion || a_bytes % 16 || b_bytes < 16 || b_bytes > kUmmaProbeRegion ||
+      b_bytes % 16)
+    return fail(LTHC_ERR_SHAPE, "operand images must be 16..%d bytes, multiples of 16", kUmmaProbeRegion);
+  if (steps < 1 || steps > kUmmaProbeMaxSteps) return fail(LTHC_ERR_SHAPE, "steps must be in [1, %d]", kUmmaProbeMaxSteps);
+  if (N < 16 || N > 256 || N % 16) return fail(LTHC_ERR_SHAPE, "N must be a multiple of 16 in [16, 256], got %d", N);
+  if (((idesc >> 24) & 31u) != 8u || ((idesc >> 17) & 63u) != static_cast<uint32_t>(N >> 3))
+    return fail(LTHC_ERR_SHAPE, "the instruction descriptor must encode M = 128 and N = %d", N);
+  UmmaProbeParams p;
+  memset(&p, 0, sizeof(p));
+  for (int s = 0; s < steps; ++s) {
+    // start addresses are region-relative and must stay inside the region (the
+    // kernel adds the region's shared address to the 14-bit field)
+    if ((a_desc[s] & 0x3FFFu) * 16 >= static_cast<uint64_t>(kUmmaProbeRegion) ||
+        (b_desc[s] & 0x3FFFu) * 16 >= static_cast<uint64_t>(kUmmaProbeRegion))
+      return fail(LTHC_ERR_SHAPE, "step %d starts outside its operand region", s);
+    p.a_desc[s] = a_desc[s];
+    p.b_desc[s] = b_desc[s];
+  }
+  p.steps = steps;
+  p.idesc = idesc;
+  p.N = N;
+  p.a_bytes = a_bytes;
+  p.b_bytes = b_bytes;
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  int per_sm = 0;
+  LTHC_TRY(resident_ctas(umma_probe_kernel, 128, kUmmaProbeSmem, &per_sm));
+  umma_probe_kernel<<<1, 128, kUmmaProbeSmem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(a_img), static_cast<const uint4*>(b_img), p, D, status_dev);
+  return launched("tcgen05 descriptor self-test");
+}
+
 // ------------------------------ write family ---------------------------------
 
 int lthc_write_fwd(const void* dz, const void* beta, int beta_dtype, void* out, int64_t B, int64_t G, int64_t C,
@@ -717,7 +863,15 @@ int lthc_materialise12_fwd(const void* x0, const void* const* dz, const void* co
 
 size_t lthc_materialise_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C, int n_layers) {
   if (B <= 0 || G <= 0 || C <= 0 || n_layers < 1 || n_layers > kMaxLayers) return 0;
-  return wgrad_ws_bytes(B, G, C, n_layers, sms_for_sizing());
+  const int sms = sms_for_sizing();
+  // the larger of the two kernels' needs (the query does not know the dtype)
+  const MbPlan m = mb_plan(B, G, C, n_layers, LTHC_DTYPE_BF16, sms);
+  return std::max(wgrad_ws_bytes(B, G, C, n_layers, sms), m.ok ? m.ws : size_t{0});
+}
+
+int lthc_materialise_bwd_uses_tensor_cores(int64_t B, int64_t G, int64_t C, int n_layers, int act_dtype) {
+  if (B < 1 || G < 1 || C < 8 || !valid_act(act_dtype)) return 0;
+  return mb_plan(B, G, C, n_layers, act_dtype, sms_for_sizing()).ok ? 1 : 0;
 }
 
 int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void* const* beta, int beta_dtype,
@@ -739,6 +893,28 @@ int lthc_materialise_bwd(const void* grad_out, const void* const* dz, const void
     if (!dz) return fail(LTHC_ERR_NULL_POINTER, "dz pointer array is NULL");
     LTHC_TRY(check_ptr(grad_beta, "grad_beta"));
     for (int l = 0; l < n_layers; ++l) LTHC_TRY(check_act(dz[l], "dz[l]", B > 0));
+  }
+  if (B == 0) {
+    ReadJob j{grad_out, beta, beta_dtype, grad_dz, dz, grad_beta, workspace, n_layers, B, G, C};
+    return read_family(j, workspace_bytes, act_dtype, static_cast<cudaStream_t>(stream));
+  }
+  int sms = 0;
+  LTHC_TRY(current_device(&sms));
+  const MbPlan m = mb_plan(B, G, C, n_layers, act_dtype, sms);
+  if (m.ok) {
+    // One pass over grad_out on the tensor cores produces both gradients.
+    if (grad_beta) {
+      if (!workspace || workspace_bytes < m.ws)
+        return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required",
+                    workspace_bytes, m.ws);
+      if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (act_dtype == LTHC_DTYPE_BF16)
+      return matbwd_tc_t<__nv_bfloat16>(m, grad_out, dz, beta, beta_dtype, n_layers, grad_dz, grad_beta, workspace,
+                                        B, G, C, s);
+    return matbwd_tc_t<__half>(m, grad_out, dz, beta, beta_dtype, n_layers, grad_dz, grad_beta, workspace, B, G, C,
+                               s);
   }
   // One pass over grad_out produces both gradients.
   ReadJob j{grad_out, beta, beta_dtype, grad_dz, dz, grad_beta, workspace, n_layers, B, G, C};

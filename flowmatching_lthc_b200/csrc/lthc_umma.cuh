@@ -166,4 +166,76 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+// ---------------------------------------------------------------------------
+// Raw-descriptor self-test: the host supplies byte images of an A and a B operand
+// region (each at most kUmmaProbeRegion bytes, copied verbatim into shared
+// memory), the shared-memory descriptors of each MMA step with start addresses
+// relative to their region, and the instruction descriptor (M = 128).  The
+// kernel adds the regions' shared addresses, issues the steps (accumulating after
+// the first) and writes D[128 x N] fp32.  This pins the no-swizzle K-major and
+// MN-major operand layouts the materialisation backward relies on.  The
+// dynamic allocation is larger than the two regions, so that a descriptor whose
+// strides reach past them still reads allocated shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kUmmaProbeRegion = 65536;
+constexpr int kUmmaProbeMaxSteps = 8;
+constexpr int kUmmaProbeSmem = 200 * 1024;
+
+struct UmmaProbeParams {
+  uint64_t a_desc[kUmmaProbeMaxSteps];
+  uint64_t b_desc[kUmmaProbeMaxSteps];
+  int steps;
+  uint32_t idesc;
+  int N;
+  int a_bytes, b_bytes;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    umma_probe_kernel(const uint4* a_img, const uint4* b_img, const __grid_constant__ UmmaProbeParams p, float* D,
+                      int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kUmmaProbeRegion;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * kUmmaProbeRegion);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int i = tid; i < 2 * kUmmaProbeRegion / 16; i += blockDim.x) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  for (int i = tid; i < p.a_bytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(sa)[i] = a_img[i];
+  for (int i = tid; i < p.b_bytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(sb)[i] = b_img[i];
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tslot, 256);
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    const uint64_t abase = smem_u32(sa) >> 4, bbase = smem_u32(sb) >> 4;
+    for (int s = 0; s < p.steps; ++s) umma_bf16(tmem, p.a_desc[s] + abase, p.b_desc[s] + bbase, p.idesc, s > 0);
+    umma_commit(bar);
+  }
+  const bool ok = mbar_wait(bar, 0);
+  tmem_fence_after_sync();
+  if (ok) {
+    const int row = 32 * warp + (tid & 31);
+    for (int c0 = 0; c0 < p.N; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + c0, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c0 + i < p.N) D[row * p.N + c0 + i] = v[i];
+    }
+  }
+  const int bad = __syncthreads_or(!ok);
+  if (tid == 0) *status = bad ? 1 : 0;
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
 }  // namespace lthc

@@ -291,6 +291,13 @@ def materialise_bwd(grad_out: Tensor, dz: list[Tensor], beta: list[Tensor], need
     return gdz, gbeta
 
 
+def materialise_bwd_uses_tensor_cores(B: int, G: int, C: int, L: int, dtype: torch.dtype) -> bool:
+    """Whether materialise_bwd runs a [B, 4G, 4G, C] gradient of this dtype with L
+    layers on the tensor cores (grad_dz then matches a sequential fp32 sum to one
+    unit in the last place of the 16-bit output)."""
+    return bool(_lib.load().lthc_materialise_bwd_uses_tensor_cores(B, G, C, L, _DTYPE_CODE[dtype]))
+
+
 @materialise_bwd.register_fake
 def _(grad_out, dz, beta, need_grad_dz, need_grad_beta):
     b, h, _, c = grad_out.shape

@@ -122,6 +122,13 @@ LTHC_API int lthc_materialise12_fwd(const void* x0, const void* const* dz, const
  * grad_dz may be NULL (weight gradient only); grad_beta may be NULL (grad_dz only).
  * The weight gradient is reduced in a fixed order: repeated calls give identical
  * bits on the same device.
+ * 16-bit activations with 2 <= n_layers, C % 16 == 0, G in {8, 16, 32} or a
+ * multiple of 32, and B*G*G a multiple of 128 run on the tensor cores
+ * (lthc_materialise_bwd_uses_tensor_cores): each fp32 beta enters as two 16-bit
+ * parts (hi + lo, 16 / 22 significant bits for bf16 / fp16) and the position sum
+ * of grad_dz is accumulated by the tensor core, so grad_dz may differ from a
+ * sequential fp32 sum by one unit in the last place of the 16-bit output on a
+ * small fraction of elements; every other case sums in fp32 in position order.
  * Replaces _backward_final_accumulate_12 (local_thc_triton_kernels.py:1897-1912):
  * jit_thc::final_accumulate_b4_12_grad_dz_ptr (:1800-1845, kernel :512-595) and
  * jit_thc::final_accumulate_b4_12_grad_beta_ptr (:1848-1894, kernel :598-680). */
@@ -131,6 +138,8 @@ LTHC_API int lthc_materialise_bwd(const void* grad_out, const void* const* dz,
                          void* const* grad_dz, float* grad_beta, void* workspace,
                          size_t workspace_bytes, int64_t B, int64_t G, int64_t C,
                          int act_dtype, void* stream);
+/* 1 if lthc_materialise_bwd runs this shape and dtype on the tensor cores, else 0. */
+LTHC_API int lthc_materialise_bwd_uses_tensor_cores(int64_t B, int64_t G, int64_t C, int n_layers, int act_dtype);
 
 /* Backward of write / write_add for one layer (grad of x_hi is grad_out itself).
  * Replaces the eager autograd of local_thc.py:1261-1276 and
@@ -223,6 +232,18 @@ LTHC_API int lthc_lazy_update_bwd(const void* grad_z_out, const void* dz, const 
  * used by the tensor-core kernels of this library. */
 LTHC_API int lthc_selftest_umma(const void* A, const void* B, float* D, int N, int K, int* status_dev,
                          void* stream);
+
+/* Raw-descriptor tensor-core self-test: a_img / b_img (device, 16-byte aligned,
+ * a_bytes / b_bytes <= 65536, multiples of 16) are copied verbatim into two
+ * shared-memory regions; then `steps` (1..8) MMAs run with the given
+ * shared-memory descriptors (host arrays; start addresses relative to their
+ * region) and instruction descriptor (M = 128, N a multiple of 16 up to 256),
+ * accumulating after the first, and D[128 x N] fp32 receives the result.
+ * *status_dev receives 0, or 1 if the bounded wait gave up.  Pins the
+ * no-swizzle operand layouts of the tensor-core materialisation backward. */
+LTHC_API int lthc_selftest_umma_desc(const void* a_img, int a_bytes, const void* b_img, int b_bytes,
+                                     const uint64_t* a_desc, const uint64_t* b_desc, int steps, uint32_t idesc,
+                                     int N, float* D, int* status_dev, void* stream);
 
 /* ======================= branch epilogue fused with the lazy update ========== */
 

@@ -12,6 +12,7 @@ import sys
 from pathlib import Path
 
 import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parent.parent
 if str(ROOT) not in sys.path:
@@ -87,3 +88,17 @@ def import_reference():
     sys.dont_write_bytecode = True  # the reference checkout may be read-only
     import flowmatching_lthc.models.local_thc as L  # noqa: F401
     return L
+
+
+def close_16bit(a: torch.Tensor, b: torch.Tensor, max_frac: float = 0.02) -> bool:
+    """a and b (same 16-bit dtype and shape) differ by at most one unit in the last
+    place (plus 1e-4 of b's largest magnitude, for sums that cancel), on at most
+    max_frac of the elements: the tolerance of the tensor-core materialisation
+    backward, whose position sums are accumulated by the tensor core."""
+    a, b = a.detach().cpu(), b.detach().cpu()
+    if a.shape != b.shape or a.dtype != b.dtype:
+        return False
+    af, bf = a.float(), b.float()
+    eps = {torch.bfloat16: 2.0**-7, torch.float16: 2.0**-10}[a.dtype]
+    bound = eps * torch.maximum(af.abs(), bf.abs()) + 1e-4 * bf.abs().max()
+    return bool(((af - bf).abs() <= bound).all()) and (af != bf).float().mean().item() <= max_frac

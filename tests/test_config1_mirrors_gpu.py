@@ -9,14 +9,15 @@ by tests/golden/make_golden.py config1; the residual-sized outputs as a fixed
 sample) within 1e-5 relative.
 
 Mirrors (local_thc_triton_kernels.py:1578-1598, 1669-1736, 1800-1894, 2673-2764)
-at L = 12, B = 2, C = 128, bf16: outputs equal the oracle bit for bit, weight
-gradients within 1e-5 relative (they sum in another order)."""
+at L = 12, B = 2, C = 128, bf16: outputs equal the oracle bit for bit (the
+tensor-core grad_dz within one unit in the last place), weight gradients within
+1e-5 relative (they sum in another order)."""
 from __future__ import annotations
 
 import pytest
 import torch
 
-from conftest import GOLDEN
+from conftest import GOLDEN, close_16bit
 from flowmatching_lthc_b200 import ops
 from flowmatching_lthc_b200 import workloads as W
 from oracle import lthc_oracle as O
@@ -84,8 +85,9 @@ def test_final_accumulate_grad_mirrors_need_no_dummy_inputs():
     g, dzd, Pd = gout.cuda(), [t.cuda() for t in dz], [p.cuda() for p in P]
     gdz = ops.final_accumulate_b4_12_grad_dz_ptr_traceable(g, *Pd)
     assert gdz.shape == (12, 2, 256, 128)
+    assert ops.materialise_bwd_uses_tensor_cores(2, 16, 128, 12, torch.bfloat16)
     for l in range(12):
-        assert bits_equal(gdz[l], rdz[l]), l
+        assert close_16bit(gdz[l], rdz[l]), l
     gb = ops.final_accumulate_b4_12_grad_beta_ptr_traceable(g, *dzd)
     assert gb.dtype == torch.float32 and gb.shape == (12, 128, 16)
     assert rel(gb, rb) < RTOL
