@@ -328,6 +328,9 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
 #ifndef LTHC_MATBWD_TC
 #define LTHC_MATBWD_TC 1  // 0: every materialisation backward runs the CUDA-core read-family kernel
 #endif
+#ifndef LTHC_MATBWD_DZ_STAGES
+#define LTHC_MATBWD_DZ_STAGES 2
+#endif
 
 // Launch plan of matbwd_tc_kernel; ok = false when the shape or dtype is not one
 // it takes (fp32, a single layer, C not a multiple of 16, a grid side that does
@@ -335,7 +338,7 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
 // 128-cell tiles): those run the CUDA-core kernel.
 struct MbPlan {
   bool ok = false;
-  int Gq = 0, Rq = 0, Lp = 0, stages = 0, visits = 0;
+  int Gq = 0, Rq = 0, Lp = 0, gstages = 0, dstages = 0, visits = 0;
   int64_t S = 0, Tc = 0, parts = 0, grid = 0;
   size_t smem = 0, ws = 0;
 };
@@ -349,12 +352,17 @@ MbPlan mb_plan(int64_t B, int64_t G, int64_t C, int L, int act, int sms) {
   m.Gq = static_cast<int>(std::min<int64_t>(G, 32));
   m.Rq = 32 / m.Gq;
   m.Lp = L + (L & 1);
-  const size_t stage = kMbGxBytes + static_cast<size_t>(L) * kMbDzLayerBytes;
-  const size_t fixed = kMbTRegion + kMbBetaBytes + kMbBarriers * 8 + 16 + 1024;  // + alignment slack
+  // two T buffers, the weight operands, a dz ring of LTHC_MATBWD_DZ_STAGES and as
+  // deep a grad X_L ring as the rest of the shared memory holds (B = 64, L = 12:
+  // 3 grad X_L + 2 dz slots)
+  const size_t dz = static_cast<size_t>(L) * kMbDzLayerBytes;
+  const size_t fixed = 2 * kMbTRegion + kMbBetaBytes + kMbBarriers * 8 + 16 + kMbSmemAlign;  // + alignment slack
   const size_t budget = 227 * 1024;
-  m.stages = static_cast<int>(std::min<size_t>(kMbMaxStages, (budget - fixed) / stage));
-  if (m.stages < 2) return m;
-  m.smem = fixed + m.stages * stage;
+  m.dstages = LTHC_MATBWD_DZ_STAGES;
+  if (fixed + m.dstages * dz > budget) return m;
+  m.gstages = static_cast<int>(std::min<size_t>(kMbMaxStages, (budget - fixed - m.dstages * dz) / kMbGxBytes));
+  if (m.gstages < 2) return m;
+  m.smem = fixed + m.dstages * dz + m.gstages * kMbGxBytes;
   m.Tc = cells / kMbTileCells;
   m.S = C / kMbSliceCh;
   // parts CTAs per slice (each a contiguous cell range), or one CTA per SM over
@@ -388,18 +396,20 @@ int matbwd_tc_t(const MbPlan& m, const void* grad_out, const void* const* dz, co
     if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (grad X_L tiles) failed with %d", (int)r);
   }
   const bool wgrad = grad_beta != nullptr;
-  bool st256 = true;
   for (int l = 0; l < L; ++l) {
     if (wgrad) p.dz[l] = dz[l];
-    if (grad_dz) st256 = st256 && (reinterpret_cast<uintptr_t>(grad_dz[l]) & 31u) == 0;
-  }
-  p.st256 = st256 ? 1 : 0;
-  for (int l = 0; l < L; ++l) {
     if (grad_dz) {
-      p.beta[l] = beta[l];
-      p.gdz[l] = grad_dz[l];
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(B * G * G)};
+      const cuuint64_t strides[1] = {C * es};
+      const cuuint32_t box[2] = {kMbSliceCh, kMbTileCells};
+      CUresult r = enc(&p.tm_gdz[l], tmap_dtype<T>(), 2, grad_dz[l], dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, kL2Promotion,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) return fail(LTHC_ERR_LAUNCH, "cuTensorMapEncodeTiled (grad_dz) failed with %d", (int)r);
     }
   }
+  for (int l = 0; l < L; ++l)
+    if (grad_dz) p.beta[l] = beta[l];
   p.partial = wgrad ? static_cast<float*>(ws) : nullptr;
   p.beta_dtype = beta_dtype;
   p.L = L;
@@ -407,7 +417,8 @@ int matbwd_tc_t(const MbPlan& m, const void* grad_out, const void* const* dz, co
   p.G = static_cast<int>(G);
   p.Gq = m.Gq;
   p.Rq = m.Rq;
-  p.stages = m.stages;
+  p.gstages = m.gstages;
+  p.dstages = m.dstages;
   p.need_pool = grad_dz != nullptr;
   p.need_wgrad = wgrad;
   p.visits = m.visits;

@@ -7,10 +7,15 @@
 // K12 :512-595, K13 :598-680).  The weights differ per channel, so the channel
 // is a batch index of both contractions, and it is the contiguous dimension in
 // HBM.  One CTA per SM walks tiles of 128 cells x 16 channels (one 32-byte
-// sector of every row); each tile arrives as four stages of 32 cells (grad X_L
-// by TMA, dz by cp.async: the TMA engine's per-row cost caps 32-byte rows near
-// 3 TB/s per GPU, so the second stream goes through the load/store unit) and
-// is transposed in shared memory (ldmatrix.trans + stmatrix) into
+// sector of every row).  CTA b owns slice b % S and cell range b / S, so the
+// CTAs that run together read every slice of the same cell rows (whole rows of
+// the residual; slice-major order left each DRAM page touched 32 bytes at a
+// time and ran at half the speed).  Each tile arrives as four stages of 32
+// cells: grad X_L by TMA into a 3-slot ring that the transposers release, dz by
+// cp.async into a 2-slot ring that GEMM 2 releases (measured faster than
+// 32-byte-row TMA boxes for dz, and it keeps the TMA engine for grad X_L).
+// grad X_L is transposed in shared memory (ldmatrix.trans + stmatrix) into one
+// of two buffers (tile parity)
 //   T[channel half][position half][8 channels][cell][8 positions]   (16-bit, no swizzle)
 // which is a K-major operand for GEMM 1 (per channel: M = 128 cells, K = 16
 // positions, N = 16 layer slots, one MMA per weight part) and an MN-major
@@ -25,12 +30,17 @@
 // the tensor core, across a CTA's tiles in fp32 in tile order (in its partial
 // buffer), and across CTAs by a fixed-order finalize: bitwise reproducible.
 //
-// Warp roles (256 threads): 0 producer (TMA), 1 MMA issuer + TMEM owner, 2-3
-// transposers (and the weight operands when the channel slice changes), 4-7
-// epilogue (TMEM -> grad_dz stores, grad_beta accumulation).  Every wait is
-// bounded; a role that gives up records the error and leaves its loop, the MMA
-// issuer drains its MMAs before TMEM is released and the producer waits for its
-// copies in flight.
+// grad_dz leaves through TMA tile stores: the epilogue packs a tile's rows into
+// that tile's T buffer (free once its MMAs completed) and hands the buffer back
+// to the transposers when the stores have read it.
+//
+// Warp roles (256 threads): 0 producer (TMA + cp.async), 1 MMA issuer + TMEM
+// owner, 2-3 transposers (and the weight operands when the channel slice
+// changes), 4-7 epilogue (TMEM -> staged grad_dz rows -> TMA stores; grad_beta
+// accumulation).  Every wait is bounded; a role that gives up records the
+// error and leaves its loop, the MMA issuer drains its MMAs before TMEM is
+// released, the producer waits for its copies in flight and the storing thread
+// for its stores.
 #pragma once
 
 #include "lthc_common.cuh"
@@ -54,22 +64,23 @@ constexpr uint32_t kMbBetaBytes = kMbSliceCh * 2 * 512;                    // 16
 constexpr int kMbThreads = 256;                    // 8 warps: at most 2 per SM sub-partition, so
                                                   // the epilogue may use up to 255 registers
 constexpr int kMbMaxStages = 6;
+constexpr uint32_t kMbSmemAlign = 128;
 constexpr int kMbTransposeWarps = 2;
 constexpr uint32_t kMbTmemCols = 512;
 constexpr uint32_t kMbD2Col = 256;
-constexpr int kMbBarriers = 3 * kMbMaxStages + 6;
+constexpr int kMbQready = 8;                      // quarter hand-offs in flight (transposers run at most 7 ahead)
+constexpr int kMbBarriers = 4 * kMbMaxStages + kMbQready + 8;
 
 struct MatBwdTcParams {
   CUtensorMap tm_gx;               // 4D (C, 4G, 4G, B), box (16, 4 Gq, 4 Rq, 1)
   const void* dz[kMaxLayers];      // [B*G*G, C]
   const void* beta[kMaxLayers];    // [C, 16]
-  void* gdz[kMaxLayers];           // [B*G*G, C]
+  CUtensorMap tm_gdz[kMaxLayers];  // grad_dz as 2D (C, B*G*G), box (16, 128): one tile's rows of a layer
   float* partial;                  // [grid][visits][L][16 channels][16 positions]
   int beta_dtype;
   int L, Lp;                       // layers, rounded up to even (GEMM-2 N = 8 Lp)
   int G, Gq, Rq;                   // cells per side; cells per box row (<= 32); cell rows per stage
-  int stages;
-  int st256;                       // grad_dz rows written as one 32-byte store (all grad_dz 32-byte aligned)
+  int gstages, dstages;             // grad X_L ring (TMA) and dz ring (cp.async) depths
   int need_pool, need_wgrad;
   int visits;                      // channel slices per CTA (at most)
   int64_t C;
@@ -183,22 +194,28 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 template <typename T>
 __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_constant__ MatBwdTcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // no-swizzle TMA boxes and descriptors need 128-byte (16-byte) alignment only
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + (kMbSmemAlign - 1)) &
+                                             ~uintptr_t(kMbSmemAlign - 1));
   const int L = p.L;
-  const uint32_t stage_bytes = kMbGxBytes + static_cast<uint32_t>(L) * kMbDzLayerBytes;
-  uint8_t* sT = smem;
-  uint8_t* sStage = smem + kMbTRegion;
-  uint8_t* sBeta = sStage + p.stages * stage_bytes;
+  const uint32_t dz_bytes = static_cast<uint32_t>(L) * kMbDzLayerBytes;
+  uint8_t* sT = smem;                                  // two T buffers (tile parity)
+  uint8_t* sGx = smem + 2 * kMbTRegion;                // grad X_L ring (TMA)
+  uint8_t* sDz = sGx + p.gstages * kMbGxBytes;         // dz ring (cp.async): [l][octet][cell][8 ch]
+  uint8_t* sBeta = sDz + p.dstages * dz_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sBeta + kMbBetaBytes);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + kMbMaxStages;
-  uint64_t* qready = bars + 2 * kMbMaxStages;
-  uint64_t* tfree = bars + 3 * kMbMaxStages;
-  uint64_t* d1full = tfree + 1;
-  uint64_t* d1empty = tfree + 2;
-  uint64_t* d2full = tfree + 3;
-  uint64_t* d2empty = tfree + 4;
-  uint64_t* drain = tfree + 5;
+  uint64_t* gfull = bars;                              // grad X_L landed (TMA transaction)
+  uint64_t* gempty = bars + kMbMaxStages;              // grad X_L transposed (transposer warps)
+  uint64_t* dfull = bars + 2 * kMbMaxStages;           // dz landed (32 lanes' copies)
+  uint64_t* dempty = bars + 3 * kMbMaxStages;          // dz consumed by GEMM 2 (MMA commit)
+  uint64_t* qready = bars + 4 * kMbMaxStages;          // [kMbQready] quarter transposed into T
+  uint64_t* tfree = qready + kMbQready;                // [2]: T buffer free again (its tile's MMAs completed)
+  uint64_t* d1full = tfree + 2;
+  uint64_t* d1empty = tfree + 3;
+  uint64_t* d2full = tfree + 4;
+  uint64_t* d2empty = tfree + 5;
+  uint64_t* drain = tfree + 6;
+  uint64_t* staged = tfree + 7;                        // grad_dz rows of a tile staged (epilogue warps)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kMbBarriers);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -208,19 +225,44 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
   const int n_q = 4 * n_tiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&full[s], p.need_wgrad ? 33 : 1);  // the TMA transaction (+ 32 lanes' dz copies)
-      mbar_init(&empty[s], 1);
-      mbar_init(&qready[s], kMbTransposeWarps);
+    for (int s = 0; s < p.gstages; ++s) {
+      mbar_init(&gfull[s], 1);
+      mbar_init(&gempty[s], kMbTransposeWarps);
     }
-    mbar_init(tfree, 1);
+    for (int s = 0; s < p.dstages; ++s) {
+      mbar_init(&dfull[s], 32);
+      mbar_init(&dempty[s], 1);
+    }
+    for (int s = 0; s < kMbQready; ++s) mbar_init(&qready[s], kMbTransposeWarps);
+    mbar_init(&tfree[0], 1);
+    mbar_init(&tfree[1], 1);
     mbar_init(d1full, 1);
     mbar_init(d1empty, 4);
     mbar_init(d2full, 1);
     mbar_init(d2empty, 4);
     mbar_init(drain, 1);
+    mbar_init(staged, 4);
     fence_barrier_init();
   }
+  // weight operands of the first slice, by every thread (independent loads):
+  // [c][part][layer group][position half][8 layers][8 positions]
+  auto build_beta = [&](int64_t slice, int t, int nthreads) {
+#pragma unroll 8
+    for (int idx = t; idx < kMbSliceCh * 16 * 16; idx += nthreads) {
+      const int c = idx >> 8, l = (idx >> 4) & 15, rr = idx & 15;
+      uint16_t hi = 0, lo = 0;
+      if (l < L) {
+        const float bv = load_weight(p.beta[l], p.beta_dtype, (slice * kMbSliceCh + c) * kPos + rr);
+        hi = to16<T>(bv);
+        lo = to16<T>(bv - from16<T>(hi));
+      }
+      const int off = c * 1024 + (l >> 3) * 256 + (rr >> 3) * 128 + (l & 7) * 16 + (rr & 7) * 2;
+      *reinterpret_cast<uint16_t*>(sBeta + off) = hi;
+      *reinterpret_cast<uint16_t*>(sBeta + off + 512) = lo;
+    }
+  };
+  if (p.need_pool && n_tiles > 0) build_beta(work.s0, threadIdx.x, kMbThreads);
+  fence_proxy_async_smem();
   if (warp == 1) tmem_alloc(tslot, kMbTmemCols);
   tmem_fence_before_sync();
   __syncthreads();
@@ -228,66 +270,71 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
   const uint32_t tmem = *tslot;
 
   if (warp == 0) {
-    // ---------------- producer: one stage per 32 cells ------------------------------
-    // lane 0: the grad X_L box by TMA; every lane: its dz pieces by cp.async, laid
-    // out [layer][channel octet][cell][8 channels] (the GEMM-2 B operand)
+    // ---------------- producer: one grad X_L box (lane 0, TMA) and one set of dz
+    // pieces (every lane, cp.async; [layer][channel octet][cell][8 channels], the
+    // GEMM-2 B operand) per quarter of 32 cells
     if (n_q > 0) {
       if (lane == 0) prefetch_tmap(&p.tm_gx);
       const uint64_t pol = policy_evict_first();
       const int64_t GG = static_cast<int64_t>(p.G) * p.G;
       const int pc = lane & 15, half = lane >> 4;  // cell (of 16) and channel octet of this lane's copies
-      int issued = 0;
+      int g_issued = 0;
       for (int Q = 0; Q < n_q; ++Q) {
-        const int s = Q % p.stages;
+        const int sg = Q % p.gstages, sd = Q % p.dstages;
         bool ok = true;
-        if (Q >= p.stages) ok = mbar_wait(&empty[s], ((Q / p.stages) & 1) ^ 1);
+        if (lane == 0 && Q >= p.gstages) ok = mbar_wait(&gempty[sg], ((Q / p.gstages) & 1) ^ 1);
         if (!__all_sync(0xffffffffu, ok)) break;
         const int64_t slice = work.slice(Q / 4, grid);
         const int64_t cell0 = work.ctile(Q / 4) * kMbTileCells + kMbQuarterCells * (Q % 4);
-        uint8_t* st = sStage + s * stage_bytes;
         if (lane == 0) {
           const int64_t b = cell0 / GG;
           const int64_t rem = cell0 - b * GG;
           const int cy = static_cast<int>(rem / p.G), cx = static_cast<int>(rem % p.G);
-          mbar_arrive_expect_tx(&full[s], kMbGxBytes);
-          tma_load_4d(st, &p.tm_gx, &full[s], static_cast<int32_t>(slice * kMbSliceCh), 4 * cx, 4 * cy,
-                      static_cast<int32_t>(b), pol);
+          mbar_arrive_expect_tx(&gfull[sg], kMbGxBytes);
+          tma_load_4d(sGx + sg * kMbGxBytes, &p.tm_gx, &gfull[sg], static_cast<int32_t>(slice * kMbSliceCh), 4 * cx,
+                      4 * cy, static_cast<int32_t>(b), pol);
         }
+        g_issued = Q + 1;
         if (p.need_wgrad) {
-          const uint32_t dst0 = smem_u32(st + kMbGxBytes) + half * 512 + pc * 16;
+          if (Q >= p.dstages) ok = mbar_wait(&dempty[sd], ((Q / p.dstages) & 1) ^ 1);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          const uint32_t dst0 = smem_u32(sDz + sd * dz_bytes) + half * 512 + pc * 16;
           const int64_t src0 = (cell0 + pc) * p.C + slice * kMbSliceCh + 8 * half;
           for (int l = 0; l < L; ++l) {
             const T* src = static_cast<const T*>(p.dz[l]) + src0;
             cp_async16(dst0 + l * kMbDzLayerBytes, src);
             cp_async16(dst0 + l * kMbDzLayerBytes + 16 * 16, src + 16 * p.C);
           }
-          cp_async_arrive(&full[s]);
+          cp_async_arrive(&dfull[sd]);
         }
-        issued = Q + 1;
       }
       // copies still in flight land before the CTA's shared memory is released
       cp_async_wait_all();
       if (lane == 0)
-        for (int Q = max(0, issued - p.stages); Q < issued; ++Q)
-          if (!mbar_wait(&full[Q % p.stages], (Q / p.stages) & 1)) break;
+        for (int Q = max(0, g_issued - p.gstages); Q < g_issued; ++Q)
+          if (!mbar_wait(&gfull[Q % p.gstages], (Q / p.gstages) & 1)) break;
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer --------------------------------------------------
     if (lane == 0 && n_q > 0) {
-      const uint32_t aT = smem_u32(sT), aSt = smem_u32(sStage), aB = smem_u32(sBeta);
+      const uint32_t aT = smem_u32(sT), aDz = smem_u32(sDz), aB = smem_u32(sBeta);
       const uint32_t idesc1 = umma_idesc_16<T>(128, 16, false, false);
       const uint32_t idesc2 = umma_idesc_16<T>(128, 8 * p.Lp, true, true);
       const uint32_t d2 = tmem + kMbD2Col;
       bool ok = true;
       for (int tt = 0; ok && tt < n_tiles; ++tt) {
+        const uint32_t aTt = aT + (tt & 1) * kMbTRegion;
         for (int q = 0; q < 4; ++q) {
-          const int Q = 4 * tt + q, s = Q % p.stages;
-          const uint32_t par = (Q / p.stages) & 1;
-          if (!mbar_wait(&full[s], par) || !mbar_wait(&qready[s], par)) {
+          const int Q = 4 * tt + q, sd = Q % p.dstages;
+          if (!mbar_wait(&qready[Q % kMbQready], (Q / kMbQready) & 1)) {
             ok = false;
             break;
           }
           if (p.need_wgrad) {
+            if (!mbar_wait(&dfull[sd], (Q / p.dstages) & 1)) {
+              ok = false;
+              break;
+            }
             if (q == 0 && tt > 0 && !mbar_wait(d2empty, (tt - 1) & 1)) {
               ok = false;
               break;
@@ -298,12 +345,12 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int ks = 0; ks < 2; ++ks) {
-                const uint64_t a = umma_desc_nosw(aT + h * kMbTGroup + (4 * q + 2 * ks) * 128, 128, kMbTChan);
-                const uint64_t bd = umma_desc_nosw(aSt + s * stage_bytes + kMbGxBytes + h * 512 + ks * 256, 128, 1024);
+                const uint64_t a = umma_desc_nosw(aTt + h * kMbTGroup + (4 * q + 2 * ks) * 128, 128, kMbTChan);
+                const uint64_t bd = umma_desc_nosw(aDz + sd * dz_bytes + h * 512 + ks * 256, 128, 1024);
                 umma_bf16(d2 + h * 8 * p.Lp, a, bd, idesc2, q > 0 || ks > 0);
               }
+            umma_commit(&dempty[sd]);  // the dz slot is free once these MMAs are done with it
           }
-          umma_commit(&empty[s]);  // the stage is free once these MMAs (and the transposers) are done with it
           if (q == 3) {
             if (p.need_wgrad) umma_commit(d2full);
             if (p.need_pool) {
@@ -317,13 +364,15 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
               for (int c = 0; c < kMbSliceCh; ++c)
 #pragma unroll
                 for (int part = 0; part < 2; ++part) {
-                  const uint64_t a = umma_desc_nosw(aT + (c >> 3) * kMbTGroup + (c & 7) * kMbTChan, kMbTHalf, 128);
+                  const uint64_t a = umma_desc_nosw(aTt + (c >> 3) * kMbTGroup + (c & 7) * kMbTChan, kMbTHalf, 128);
                   const uint64_t bd = umma_desc_nosw(aB + c * 1024 + part * 512, 128, 256);
                   umma_bf16(tmem + c * 16, a, bd, idesc1, part > 0);
                 }
               umma_commit(d1full);
             }
-            umma_commit(tfree);
+            // with grad_dz the epilogue releases T after its stores have read the rows
+            // it staged there; without, T is free when these MMAs complete
+            if (!p.need_pool) umma_commit(&tfree[tt & 1]);
           }
         }
       }
@@ -340,40 +389,35 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
     const uint32_t src_lane = static_cast<uint32_t>(((r >> 2) * 4 * p.Gq + (r & 3)) * 32 + octet * 16);
     const uint32_t dst_lane = static_cast<uint32_t>(octet * kMbTGroup + rhalf * kMbTHalf + row * kMbTChan);
     const int tid_t = threadIdx.x - 64;  // 0 .. 32 * kMbTransposeWarps - 1
-    int64_t cur_slice = -1;
+    int64_t cur_slice = work.s0;  // its weight operands were built at the start
     bool ok = true;
     for (int tt = 0; ok && tt < n_tiles; ++tt) {
       const int64_t slice = work.slice(tt, grid);
+      const uint32_t aTt = aT + (tt & 1) * kMbTRegion;
       for (int q = 0; q < 4; ++q) {
-        const int Q = 4 * tt + q, s = Q % p.stages;
-        if (!mbar_wait(&full[s], (Q / p.stages) & 1)) {
+        const int Q = 4 * tt + q, sg = Q % p.gstages;
+        if (!mbar_wait(&gfull[sg], (Q / p.gstages) & 1)) {
           ok = false;
           break;
         }
         if (q == 0) {
-          // T (and the weight operands) are rewritten only after the previous tile's MMAs completed
-          if (tt > 0 && !mbar_wait(tfree, (tt - 1) & 1)) {
+          // this T buffer is rewritten only after the MMAs of its previous tile (tt - 2) completed
+          if (tt >= 2 && !mbar_wait(&tfree[tt & 1], ((tt >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
           if (p.need_pool && slice != cur_slice) {
-            // weight operands of this slice: [c][part][layer group][position half][8 layers][8 positions]
-            for (int idx = tid_t; idx < kMbSliceCh * 16 * 16; idx += 32 * kMbTransposeWarps) {
-              const int c = idx >> 8, l = (idx >> 4) & 15, rr = idx & 15;
-              uint16_t hi = 0, lo = 0;
-              if (l < L) {
-                const float bv = load_weight(p.beta[l], p.beta_dtype, (slice * kMbSliceCh + c) * kPos + rr);
-                hi = to16<T>(bv);
-                lo = to16<T>(bv - from16<T>(hi));
-              }
-              const int off = c * 1024 + (l >> 3) * 256 + (rr >> 3) * 128 + (l & 7) * 16 + (rr & 7) * 2;
-              *reinterpret_cast<uint16_t*>(sBeta + off) = hi;
-              *reinterpret_cast<uint16_t*>(sBeta + off + 512) = lo;
+            // a new slice's weight operands replace the old ones once the last tile
+            // of the old slice (tt - 1, the other buffer) has completed too
+            if (!mbar_wait(&tfree[(tt - 1) & 1], ((tt - 1) >> 1) & 1)) {
+              ok = false;
+              break;
             }
+            build_beta(slice, tid_t, 32 * kMbTransposeWarps);
             cur_slice = slice;
           }
         }
-        const uint32_t st = smem_u32(sStage + s * stage_bytes) + src_lane;
+        const uint32_t st = smem_u32(sGx + sg * kMbGxBytes) + src_lane;
         // all loads of this warp's cells first, then all stores: the loads overlap
         // instead of each store waiting for its own load
         constexpr int kCells = kMbQuarterCells / kMbTransposeWarps;
@@ -386,10 +430,13 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
         }
 #pragma unroll
         for (int k = 0; k < kCells; ++k)
-          stsm_x4(aT + dst_lane + static_cast<uint32_t>((kMbQuarterCells * q + kCells * w + k) * 16), v[k]);
+          stsm_x4(aTt + dst_lane + static_cast<uint32_t>((kMbQuarterCells * q + kCells * w + k) * 16), v[k]);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&qready[s]);
+        if (lane == 0) {
+          mbar_arrive(&gempty[sg]);  // the grad X_L slot has been read
+          mbar_arrive(&qready[Q % kMbQready]);
+        }
       }
     }
   } else {
@@ -455,7 +502,10 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
           break;
         }
         tmem_fence_after_sync();
-        const int64_t cell = ctile * kMbTileCells + 32 * lq + lane;
+        // the tile's T buffer (free: GEMM 1 and 2 of this tile have completed) stages
+        // the packed rows as [layer][cell][16 channels] for the TMA tile stores
+        uint8_t* const stg = sT + (tt & 1) * kMbTRegion;
+        const uint32_t row_lane = smem_u32(stg) + (32 * lq + lane) * (kMbSliceCh * 2);
         // two passes of half the layers each (the packed rows of all layers at once
         // would not fit in registers)
         constexpr int kHalfL = (kMaxLayers + 1) / 2;
@@ -483,26 +533,42 @@ __global__ void __launch_bounds__(kMbThreads, 1) matbwd_tc_kernel(const __grid_c
             for (int j = 0; j < kHalfL; ++j) {
               const int l = lh * kHalfL + j;
               if (l < L) {
-                T* row = static_cast<T*>(p.gdz[l]) + cell * p.C + slice * kMbSliceCh;
-                if (p.st256) {
-                  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(row), "r"(o[j][0]),
-                               "r"(o[j][1]), "r"(o[j][2]), "r"(o[j][3]), "r"(o[j][4]), "r"(o[j][5]), "r"(o[j][6]),
-                               "r"(o[j][7])
-                               : "memory");
-                } else {
-                  uint4* dst = reinterpret_cast<uint4*>(row);
-                  dst[0] = make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]);
-                  dst[1] = make_uint4(o[j][4], o[j][5], o[j][6], o[j][7]);
-                }
+                const uint32_t a = row_lane + l * (kMbTileCells * kMbSliceCh * 2);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(o[j][0]), "r"(o[j][1]),
+                             "r"(o[j][2]), "r"(o[j][3])
+                             : "memory");
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a + 16), "r"(o[j][4]), "r"(o[j][5]),
+                             "r"(o[j][6]), "r"(o[j][7])
+                             : "memory");
               }
             }
           }
         }
         tmem_fence_before_sync();
+        fence_proxy_async_smem();  // the staged rows are read by the TMA engine
         __syncwarp();
-        if (lane == 0) mbar_arrive(d1empty);
+        if (lane == 0) {
+          mbar_arrive(d1empty);
+          mbar_arrive(staged);
+        }
+        if (warp == 4 && lane == 0) {
+          // one thread stores the tile's L row blocks and, once they have been read
+          // from shared memory, hands the T buffer back to the transposers
+          if (!mbar_wait(staged, tt & 1)) {
+            ok = false;
+            break;
+          }
+#pragma unroll 1
+          for (int l = 0; l < L; ++l)
+            tma_store_2d(&p.tm_gdz[l], stg + l * (kMbTileCells * kMbSliceCh * 2), static_cast<int32_t>(slice * kMbSliceCh),
+                         static_cast<int32_t>(ctile * kMbTileCells));
+          bulk_commit();
+          bulk_wait_read<0>();
+          mbar_arrive(&tfree[tt & 1]);
+        }
       }
     }
+    if (warp == 4 && lane == 0) bulk_wait_all();  // the stores have completed before the CTA exits
   }
   tmem_fence_before_sync();
   __syncthreads();
