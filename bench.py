@@ -275,12 +275,12 @@ def op_step(op: str, cfg: dict):
         "materialise_fwd": (lambda: ops.call(ops.materialise, x0, dz, P), W.materialise_bytes(B, G, C, L, 2), 1,
                             "broadcast_tma_kernel<bf16, 12, base>"),
         "materialise_bwd": (lambda: ops.call(ops.materialise_bwd, g, dz, P, True, True), W.materialise_bwd_bytes(B, G, C, L, 2), 2,
-                            "pool_tma_kernel<bf16, 12, pool, wgrad> + reduce_partials_kernel"),
+                            "matbwd_tc_kernel<bf16> + matbwd_tc_finalize_kernel"),
         "materialise_grad_dz": (lambda: ops.call(ops.materialise_grad_dz, g, P), W.materialise_grad_dz_bytes(B, G, C, L, 2),
-                                1, "pool_tma_kernel<bf16, 12, pool>"),
+                                1, "matbwd_tc_kernel<bf16> (grad_dz only)"),
         "materialise_grad_beta": (lambda: ops.call(ops.materialise_grad_beta, g, dz),
                                   W.materialise_grad_beta_bytes(B, G, C, L, 2), 2,
-                                  "pool_tma_kernel<bf16, 12, wgrad> + reduce_partials_kernel"),
+                                  "matbwd_tc_kernel<bf16> (grad_beta only) + matbwd_tc_finalize_kernel"),
         "read_fwd": (lambda: ops.call(ops.read, x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
         "read_bwd": (lambda: ops.call(ops.read_bwd, x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
                      "broadcast_tma_kernel<bf16, 1> + pool_tma_kernel<bf16, 1, wgrad> + reduce_partials_kernel"),
