@@ -282,8 +282,8 @@ def op_step(op: str, cfg: dict):
                                   W.materialise_grad_beta_bytes(B, G, C, L, 2), 2,
                                   "matbwd_tc_kernel<bf16> (grad_beta only) + matbwd_tc_finalize_kernel"),
         "read_fwd": (lambda: ops.call(ops.read, x0, alpha), W.read_bytes(B, G, C, 2, 2), 1, "pool_tma_kernel<bf16, 1, pool>"),
-        "read_bwd": (lambda: ops.call(ops.read_bwd, x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 3,
-                     "broadcast_tma_kernel<bf16, 1> + pool_tma_kernel<bf16, 1, wgrad> + reduce_partials_kernel"),
+        "read_bwd": (lambda: ops.call(ops.read_bwd, x0, z, alpha, True, True), W.read_bwd_bytes(B, G, C, 2, 2), 2,
+                     "broadcast_tma_kernel<bf16, 1, wgrad> (one pass) + reduce_partials_kernel"),
         "write_add_fwd": (lambda: ops.call(ops.write_add, x0, dz[0], beta), W.write_add_bytes(B, G, C, 2, 2), 1,
                           "broadcast_tma_kernel<bf16, 1, base>"),
         "lazy_fwd": (lambda: ops.call(ops.lazy_update, z, dz[0], alpha, beta), W.lazy_bytes(B * G * G, C, 2, 2), 1,

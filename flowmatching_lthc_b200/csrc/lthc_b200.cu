@@ -153,9 +153,24 @@ int64_t one_wave_columns(int64_t strips, int64_t C, int sms, int per_sm) {
 
 int64_t wgrad_blocks(int64_t strips, int64_t C, int sms) { return one_wave_columns(strips, C, sms, kWgradCtasPerSm); }
 
+// CTA columns of the one-pass read backward (one partial block per column): one
+// wave of its resident CTAs (BcastShape<1, base, true>).
+int64_t read_bwd_blocks(int64_t strips, int64_t C, int sms, bool base) {
+  return one_wave_columns(strips, C, sms, base ? LTHC_READBWD_BASE_CTAS_PER_SM : LTHC_READBWD_CTAS_PER_SM);
+}
+
 size_t wgrad_ws_bytes(int64_t B, int64_t G, int64_t C, int L, int sms) {
   if (B <= 0) return 0;
   return static_cast<size_t>(wgrad_blocks(strips_of(B, G), C, sms)) * L * C * kPos * sizeof(float);
+}
+
+// Workspace of the read backward: the partials of the one-pass kernel or of the
+// weight-gradient kernel, whichever the call uses.
+size_t read_bwd_ws_bytes(int64_t B, int64_t G, int64_t C, int sms) {
+  if (B <= 0) return 0;
+  const int64_t nx = std::max(read_bwd_blocks(strips_of(B, G), C, sms, true),
+                              read_bwd_blocks(strips_of(B, G), C, sms, false));
+  return std::max(static_cast<size_t>(nx) * C * kPos * sizeof(float), wgrad_ws_bytes(B, G, C, 1, sms));
 }
 
 // Lazy-update grid: CTAs of 8 warps over (row blocks) x (channel slices of 32
@@ -272,19 +287,53 @@ int resident_ctas(Kernel kern, int threads, int smem_bytes, int* out) {
 }
 
 // ---- dispatch helpers -----------------------------------------------------
-template <typename T, int LT, bool HB>
-int launch_broadcast_tma(BcastTmaParams& p, int sms, cudaStream_t s) {
-  using Lay = BcastLayout<T, LT, HB>;
+template <typename T, int LT, bool HB, bool WG = false>
+int launch_broadcast_tma(BcastTmaParams& p, int sms, cudaStream_t s, int64_t* nx_out = nullptr) {
+  using Lay = BcastLayout<T, LT, HB, WG>;
   constexpr int kThreads = Lay::Shape::kThreads;
-  auto kern = broadcast_tma_kernel<T, LT, HB>;
+  auto kern = broadcast_tma_kernel<T, LT, HB, WG>;
   int per_sm = 1;
   LTHC_TRY(resident_ctas(kern, kThreads, Lay::kSmemBytes, &per_sm));
   const int64_t slices = slices_of(p.C);
-  int64_t nx = one_wave_columns(p.strips, p.C, sms, per_sm);
+  // the fused read backward writes one partial block per CTA column: the
+  // weight-gradient grid, which the workspace query sizes
+  int64_t nx = WG ? read_bwd_blocks(p.strips, p.C, sms, HB) : one_wave_columns(p.strips, p.C, sms, per_sm);
   p.strips_per_cta = ceil_div(p.strips, nx);
   nx = ceil_div(p.strips, p.strips_per_cta);
+  if (nx_out) *nx_out = nx;
   kern<<<dim3(static_cast<unsigned>(nx), static_cast<unsigned>(slices)), kThreads, Lay::kSmemBytes, s>>>(p);
-  return launched("broadcast (TMA)");
+  return launched(WG ? "read backward (TMA, one pass)" : "broadcast (TMA)");
+}
+
+// grad_x = (grad_x_in +) alpha (.) grad_z and grad_alpha in one pass over x.
+template <typename T>
+int read_bwd_fused_t(const void* x, const void* grad_z, const void* alpha, int alpha_dtype, const void* grad_x_in,
+                     void* grad_x, float* grad_alpha, void* ws, int64_t B, int64_t G, int64_t C, int sms,
+                     cudaStream_t s) {
+  BcastTmaParams p;
+  memset(&p, 0, sizeof(p));
+  if (grad_x_in) LTHC_TRY(encode_residual_map<T>(&p.tm_base, grad_x_in, B, G, C));
+  LTHC_TRY(encode_residual_map<T>(&p.tm_out, grad_x, B, G, C));
+  LTHC_TRY(encode_residual_map<T>(&p.tm_x, x, B, G, C));
+  LTHC_TRY(encode_workspace_map<T>(&p.tm_dz[0], grad_z, B * G * G, C));
+  p.w[0] = alpha;
+  p.partial = static_cast<float*>(ws);
+  p.out = grad_x;
+  p.w_dtype = alpha_dtype;
+  p.L = 1;
+  p.G = static_cast<int>(G);
+  p.strips_per_row = static_cast<int>(ceil_div(G, kStripCells));
+  p.C = C;
+  p.strips = B * G * p.strips_per_row;
+  int64_t nx = 0;
+  if (grad_x_in)
+    LTHC_TRY((launch_broadcast_tma<T, 1, true, true>(p, sms, s, &nx)));
+  else
+    LTHC_TRY((launch_broadcast_tma<T, 1, false, true>(p, sms, s, &nx)));
+  const int64_t n = C * kPos;
+  const int64_t rb = std::min<int64_t>(ceil_div(n, 256), static_cast<int64_t>(sms) * 8);
+  reduce_partials_kernel<<<static_cast<unsigned>(rb), 256, 0, s>>>(p.partial, grad_alpha, n, static_cast<int>(nx));
+  return launched("weight-grad reduce");
 }
 
 template <typename T>
@@ -1032,7 +1081,8 @@ int lthc_weight_grad_noalloc(const void* high, const void* const* low, int n_lay
 }
 
 size_t lthc_read_bwd_workspace_bytes(int64_t B, int64_t G, int64_t C) {
-  return lthc_materialise_bwd_workspace_bytes(B, G, C, 1);
+  if (B <= 0 || G <= 0 || C <= 0) return 0;
+  return read_bwd_ws_bytes(B, G, C, sms_for_sizing());
 }
 
 int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alpha_dtype, const void* grad_x_in,
@@ -1049,13 +1099,30 @@ int lthc_read_bwd(const void* x, const void* grad_z, const void* alpha, int alph
     // validate the workspace before anything is enqueued
     int sms = 0;
     LTHC_TRY(current_device(&sms));
-    const size_t need = wgrad_ws_bytes(B, G, C, 1, sms);
+    const size_t need = grad_x ? read_bwd_ws_bytes(B, G, C, sms) : wgrad_ws_bytes(B, G, C, 1, sms);
     if (B > 0 && (!workspace || workspace_bytes < need))
       return fail(LTHC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes required", workspace_bytes,
                   need);
   }
+  if (grad_x) LTHC_TRY(check_act(grad_x, "grad_x", B > 0));
+  if (grad_x && grad_alpha && B > 0) {
+    // both gradients: one pass reads x and grad_z once and writes grad_x
+    if (!aligned16(workspace)) return fail(LTHC_ERR_ALIGNMENT, "workspace is not 16-byte aligned");
+    int sms = 0;
+    LTHC_TRY(current_device(&sms));
+    switch (act_dtype) {
+      case LTHC_DTYPE_F32:
+        return read_bwd_fused_t<float>(x, grad_z, alpha, alpha_dtype, grad_x_in, grad_x, grad_alpha, workspace, B, G,
+                                       C, sms, s);
+      case LTHC_DTYPE_BF16:
+        return read_bwd_fused_t<__nv_bfloat16>(x, grad_z, alpha, alpha_dtype, grad_x_in, grad_x, grad_alpha,
+                                               workspace, B, G, C, sms, s);
+      default:
+        return read_bwd_fused_t<__half>(x, grad_z, alpha, alpha_dtype, grad_x_in, grad_x, grad_alpha, workspace, B,
+                                        G, C, sms, s);
+    }
+  }
   if (grad_x) {
-    LTHC_TRY(check_act(grad_x, "grad_x", B > 0));
     if (B > 0) {
       const void* dzs[1] = {grad_z};
       const void* ws[1] = {alpha};

@@ -1,6 +1,10 @@
 // Write family on the TMA pipeline: out = base + sum_{l<L} w_l (.) dz_l broadcast
 // over each 4x4 cell (write, write_add, the fused materialisation and the read
-// backward's grad_x).
+// backward's grad_x).  The WGRAD variant is the whole read backward in one pass:
+// its stages also carry the x tile, and the consumers add x (.) grad_z into
+// per-lane sums that become one partial block per CTA (the read's grad_alpha,
+// reduced in CTA order by reduce_partials_kernel), so x and grad_z are each read
+// once.
 //
 // CTA = consumer warps + 1 producer warp, owning one 64-channel slice of the
 // residual.  The producer's elected lane streams "strips" of kStripCells
@@ -73,27 +77,49 @@ constexpr int kBoxCols = 4 * kStripCells;
 #ifndef LTHC_BCAST_BASE_STORE_LAG
 #define LTHC_BCAST_BASE_STORE_LAG 2
 #endif
-template <int LT, bool HAS_BASE>
+// The read backward in one pass (WGRAD): grad_x = (grad_x_in +) alpha (.) grad_z and
+// grad_alpha partials from x; its stages also carry the x tile.  Measured on B200
+// at B = 64 bf16: without grad_x_in one CTA per SM with 12 stages (139 us against
+// 171 us for two CTAs with 6); with grad_x_in (three residual streams) two CTAs
+// with 6 (225 us against 244 us).
+#ifndef LTHC_READBWD_STAGES_16BIT
+#define LTHC_READBWD_STAGES_16BIT 12
+#endif
+#ifndef LTHC_READBWD_CTAS_PER_SM
+#define LTHC_READBWD_CTAS_PER_SM 1
+#endif
+#ifndef LTHC_READBWD_BASE_STAGES_16BIT
+#define LTHC_READBWD_BASE_STAGES_16BIT 6
+#endif
+#ifndef LTHC_READBWD_BASE_CTAS_PER_SM
+#define LTHC_READBWD_BASE_CTAS_PER_SM 2
+#endif
+template <int LT, bool HAS_BASE, bool WGRAD = false>
 struct BcastShape {
-  static constexpr bool kSingle = LT == 1 && HAS_BASE;
+  static constexpr bool kSingle = LT == 1 && HAS_BASE && !WGRAD;
   static constexpr int kCols = kSingle ? LTHC_BCAST1_COLS : LTHC_BCAST_COLS;  // cell columns per consumer warp
   static constexpr int kWarpsPerRow = 4 / kCols;
   static_assert(kCols * kWarpsPerRow == 4, "columns per warp must divide 4");
   static constexpr int kConsumerWarps = 4 * kWarpsPerRow;
   static constexpr int kThreads = 32 * (kConsumerWarps + 1);
-  static constexpr int kMinBlocks = kSingle ? LTHC_BCAST1_MIN_BLOCKS : LTHC_BCAST_MIN_BLOCKS;
-  static constexpr int kStages16 = kSingle ? LTHC_BCAST1_STAGES_16BIT : LTHC_BCAST_STAGES_16BIT;
+  static constexpr int kMinBlocks =
+      WGRAD ? (HAS_BASE ? LTHC_READBWD_BASE_CTAS_PER_SM : LTHC_READBWD_CTAS_PER_SM)
+            : (kSingle ? LTHC_BCAST1_MIN_BLOCKS : LTHC_BCAST_MIN_BLOCKS);
+  static constexpr int kStages16 =
+      WGRAD ? (HAS_BASE ? LTHC_READBWD_BASE_STAGES_16BIT : LTHC_READBWD_STAGES_16BIT)
+            : (kSingle ? LTHC_BCAST1_STAGES_16BIT : LTHC_BCAST_STAGES_16BIT);
   // Output tile stores a CTA keeps in flight before it recycles a stage.
   static constexpr int kStoreLag = HAS_BASE ? LTHC_BCAST_BASE_STORE_LAG : LTHC_BCAST_NOBASE_STORE_LAG;
 };
 
-template <typename T, int LT, bool HAS_BASE>
+template <typename T, int LT, bool HAS_BASE, bool WGRAD = false>
 struct BcastLayout {
-  using Shape = BcastShape<LT, HAS_BASE>;
+  using Shape = BcastShape<LT, HAS_BASE, WGRAD>;
   static constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
   static constexpr int kBaseBytes = 4 * kBoxCols * kSliceCh * static_cast<int>(sizeof(T));
   static constexpr int kDzTileBytes = kStripCells * kSliceCh * static_cast<int>(sizeof(T));
-  static constexpr int kStageBytes = kBaseBytes + LMAX * kDzTileBytes;
+  static constexpr int kXOffset = kBaseBytes + LMAX * kDzTileBytes;  // x tile (WGRAD)
+  static constexpr int kStageBytes = kXOffset + (WGRAD ? kBaseBytes : 0);
   static constexpr int kStages = sizeof(T) == 2 ? Shape::kStages16 : (Shape::kStages16 + 1) / 2;
   static_assert(Shape::kStoreLag >= 1 && Shape::kStoreLag < kStages, "store lag must be below the stage count");
   static constexpr int kBarrierOffset = kStages * kStageBytes;
@@ -105,7 +131,9 @@ struct BcastTmaParams {
   CUtensorMap tm_base;                 // 4D (C, 4G, 4G, B) box (64, 16, 4, 1); unused without a base
   CUtensorMap tm_out;                  // 4D map of the output, same box
   CUtensorMap tm_dz[kMaxLayers];       // 2D (C, B*G*G) box (64, 4)
+  CUtensorMap tm_x;                    // WGRAD: 4D map of x, same box
   const void* w[kMaxLayers];           // [C, 16] weights, dtype w_dtype
+  float* partial;                      // WGRAD: [gridDim.x][C][16] per-CTA sums of x (.) grad_z
   void* out;                           // T[B, 4G, 4G, C]
   int w_dtype;
   int L;
@@ -144,11 +172,13 @@ struct StripCursor {
   }
 };
 
-template <typename T, int LT, bool HAS_BASE>
-__global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape<LT, HAS_BASE>::kMinBlocks)
+template <typename T, int LT, bool HAS_BASE, bool WGRAD = false>
+__global__ void __launch_bounds__(BcastShape<LT, HAS_BASE, WGRAD>::kThreads,
+                                  BcastShape<LT, HAS_BASE, WGRAD>::kMinBlocks)
     broadcast_tma_kernel(const __grid_constant__ BcastTmaParams p) {
   constexpr int LMAX = LT > 0 ? LT : kMaxLayers;
-  using Lay = BcastLayout<T, LT, HAS_BASE>;
+  static_assert(!WGRAD || LT == 1, "the fused read backward has one update (grad_z)");
+  using Lay = BcastLayout<T, LT, HAS_BASE, WGRAD>;
   using Shape = typename Lay::Shape;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -176,10 +206,12 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape
     // ---------------- producer: one elected lane issues every TMA load ----------
     if (lane == 0) {
       if constexpr (HAS_BASE) prefetch_tmap(&p.tm_base);
+      if constexpr (WGRAD) prefetch_tmap(&p.tm_x);
       for (int l = 0; l < LMAX; ++l)
         if (l < L) prefetch_tmap(&p.tm_dz[l]);
       const uint64_t pol = policy_evict_first();
-      const uint32_t tx = (HAS_BASE ? Lay::kBaseBytes : 0) + static_cast<uint32_t>(L) * Lay::kDzTileBytes;
+      const uint32_t tx = (HAS_BASE ? Lay::kBaseBytes : 0) + static_cast<uint32_t>(L) * Lay::kDzTileBytes +
+                          (WGRAD ? Lay::kBaseBytes : 0);
       const int64_t GG = static_cast<int64_t>(p.G) * p.G;
       int issued = 0;
       StripCursor cur(s_begin, p.G, p.strips_per_row);
@@ -194,6 +226,9 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape
         if constexpr (HAS_BASE)
           tma_load_4d(st, &p.tm_base, &full[s], static_cast<int32_t>(c0), 4 * wx0, 4 * wy, static_cast<int32_t>(b),
                       pol);
+        if constexpr (WGRAD)
+          tma_load_4d(st + Lay::kXOffset, &p.tm_x, &full[s], static_cast<int32_t>(c0), 4 * wx0, 4 * wy,
+                      static_cast<int32_t>(b), pol);
         const int32_t row0 = static_cast<int32_t>(b * GG + static_cast<int64_t>(wy) * p.G + wx0);
 #pragma unroll
         for (int l = 0; l < LMAX; ++l)
@@ -234,6 +269,9 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape
   const uint32_t smem_base = smem_u32(smem);
   constexpr uint32_t kEs = sizeof(T);
   const bool storer = warp == 0 && lane == 0;
+  float2 accw[kCols];  // WGRAD: sum over cells of x (.) grad_z for this lane's columns, in strip order
+#pragma unroll
+  for (int col = 0; col < kCols; ++col) accw[col] = make_float2(0.f, 0.f);
   StripCursor cur(s_begin, p.G, p.strips_per_row);
 
   for (int it = 0; it < n_it; ++it, cur.next()) {
@@ -257,6 +295,12 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape
           const float2 d = lds_pair<T>(sb + Lay::kBaseBytes + ((l * kStripCells + k) * kSliceCh + 2 * lane) * kEs);
 #pragma unroll
           for (int col = 0; col < kCols; ++col) acc[col] = ffma2(w[l][col], d, acc[col]);
+          if constexpr (WGRAD) {
+            // cells past the grid edge are zero in both tiles (TMA fill), so they add nothing
+#pragma unroll
+            for (int col = 0; col < kCols; ++col)
+              accw[col] = ffma2(lds_pair<T>(xa + Lay::kXOffset + col * kSliceCh * kEs), d, accw[col]);
+          }
         }
       }
 #pragma unroll
@@ -271,6 +315,16 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE>::kThreads, BcastShape
       // The store issued kStoreLag strips ago has read its tile: recycle that stage.
       bulk_wait_read<Shape::kStoreLag>();
       if (it >= Shape::kStoreLag) mbar_arrive(&empty[(it - Shape::kStoreLag) % Lay::kStages]);
+    }
+  }
+  if constexpr (WGRAD) {
+    if (cvalid) {
+      float* P = p.partial + static_cast<int64_t>(blockIdx.x) * p.C * kPos;
+#pragma unroll
+      for (int col = 0; col < kCols; ++col) {
+        P[c * kPos + row * 4 + col0 + col] = accw[col].x;
+        P[(c + 1) * kPos + row * 4 + col0 + col] = accw[col].y;
+      }
     }
   }
   if (storer) bulk_wait_all();

@@ -118,11 +118,11 @@ def write_add_bytes(B: int, G: int, C: int, act_bytes: int, w_bytes: int) -> int
 
 
 def read_bwd_bytes(B: int, G: int, C: int, act_bytes: int, w_bytes: int) -> int:
-    """grad_x = alpha (.) grad_z (write grad_x, read grad_z) plus grad_alpha = sum x*grad_z
-    (read x, read grad_z, write the fp32 [C,16] gradient)."""
+    """grad_x = alpha (.) grad_z and grad_alpha = sum x*grad_z in one pass: read x and
+    grad_z once, write grad_x and the fp32 [C,16] gradient."""
     hi = B * 16 * G * G * C
     lo = B * G * G * C
-    return (2 * hi + 2 * lo) * act_bytes + C * 16 * (w_bytes + 4)
+    return (2 * hi + lo) * act_bytes + C * 16 * (w_bytes + 4)
 
 
 def lazy_bytes(N: int, C: int, act_bytes: int, w_bytes: int) -> int:

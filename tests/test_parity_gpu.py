@@ -184,6 +184,11 @@ def test_read_backward(dt, B, G, C):
     gx2, ga2 = ops.read_bwd(x.cuda(), gz.cuda(), a.cuda(), True, True, base.cuda())
     assert same_bits(gx2, O.write_add(base, gz, a))
     assert torch.equal(ga2, ga)
+    # both gradients come from one fused pass; either alone from the write / weight-gradient kernels
+    gx_only, _ = ops.read_bwd(x.cuda(), gz.cuda(), a.cuda(), True, False)
+    _, ga_only = ops.read_bwd(x.cuda(), gz.cuda(), a.cuda(), False, True)
+    assert same_bits(gx_only, gx)
+    assert rel_err(ga_only, ga) < RTOL_REDUCTION
 
 
 @pytest.mark.parametrize("dt", DTYPES)
