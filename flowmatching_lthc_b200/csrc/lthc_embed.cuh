@@ -258,8 +258,10 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
                   umma_desc_sw128(sbase + EmbedSmem::kW2 + (s >> 2) * 32768 + 32 * (s & 3)), idesc2, s > 0);
       umma_commit(bar2);
     }
-    // the next tile's patches into A1 (GEMM 1 of this tile has completed) while GEMM 2 runs
+    // the next tile's patches into A1 (GEMM 1 of this tile has completed) while GEMM 2
+    // runs, and at once the loads of the tile after it: a whole iteration to land
     if (has_next) gather_store(pre);
+    if (tile + 2 * ctas_per_chunk < p.tiles) gather_load(tile + 2 * ctas_per_chunk);
     ok = mbar_wait(bar2, it & 1);
     tmem_fence_after_sync();
 
@@ -299,7 +301,6 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
 
     // ---- GEMM 1 of the next tile (its patches are staged, D1 was read by epilogue 1)
     if (has_next) issue_gemm1();
-    if (tile + 2 * ctas_per_chunk < p.tiles) gather_load(tile + 2 * ctas_per_chunk);
 
     // ---- X0 out: four TMA tile stores of 64 channels x 32 columns x 4 rows
     if (tid == 0) {
