@@ -307,11 +307,14 @@ __global__ void __launch_bounds__(BcastShape<LT, HAS_BASE, WGRAD>::kThreads,
       for (int col = 0; col < kCols; ++col) sts_pair<T>(xa + col * kSliceCh * kEs, acc[col]);
     }
     fence_proxy_async_smem();
-    // All consumer warps wait on the same stage transaction: a warp leaves the loop
-    // at a stage only when that transaction never completed, and then every warp
-    // waiting on it gives up as well (the producer stops issuing once its own
-    // bounded wait fails).  A bounded mbarrier hand-off here, or bar.red.and,
-    // measured 6-14 % slower on the single-layer shapes (write_add, read backward).
+    // All consumer warps wait on the same stage transaction, with 2-second limits
+    // that start within microseconds of each other: a warp leaves the loop when that
+    // transaction has not completed for 2 s, and the others give up with it unless
+    // the transaction completes inside those microseconds (the producer stops
+    // issuing once its own bounded wait fails, so a stalled pipeline does not
+    // recover).  A bounded mbarrier hand-off here, or bar.red.and, would close that
+    // window but measured 6-14 % slower on the single-layer shapes (write_add,
+    // read backward).
     named_barrier(1, 32 * Shape::kConsumerWarps);
     if (storer) {
       tma_store_4d(&p.tm_out, smem + s * Lay::kStageBytes, static_cast<int32_t>(c0), 4 * cur.wx0(), 4 * cur.wy,
