@@ -429,11 +429,19 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
         ms = _timed(step, 10, stream)
         return {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_step": round(ms / 10, 3)}
 
-    # ours: gradients accumulate into one flat buffer, one all-reduce (mean) per step
+    # ours: gradients accumulate into one flat buffer, one all-reduce (mean) per step;
+    # forward + backward and the update replayed from two CUDA graphs (the exchange
+    # runs eagerly between them); the same step eagerly for comparison
+    from flowmatching_lthc_b200.training import GraphedTrainStep, flow_matching_step
     m.train()
-    opt = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True)
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-4, fused=True, capturable=True)
     fg = D.FlatGradients(m.parameters())
-    leg["ours"] = timed_train(make_step(m, opt, fg.zero_grad, fg.allreduce))
+    eager = timed_train(make_step(m, opt, fg.zero_grad, fg.allreduce))
+    graphed = GraphedTrainStep(flow_matching_step(m, fg.zero_grad, zt, t, y, v), opt.step)
+    leg["ours"] = timed_train(lambda: graphed(fg.allreduce))
+    leg["ours"]["path"] = "forward + backward and the AdamW update replayed from two CUDA graphs, exchange eager"
+    leg["ours"]["eager"] = eager
+    del graphed  # release the graphs' memory pool before the comparison steps
     if r.world > 1:
         # the same step without any exchange, one bare all-reduce of the gradient bytes,
         # and PyTorch's DistributedDataParallel (bucketed all-reduces during backward)
