@@ -399,6 +399,25 @@ def model_legs(r: D.Rank, dev, stream, reference_gpu: bool = False) -> dict:
             fwd()
         ms = _timed(fwd, 10, stream)
         leg[tag] = {"images_per_s": round(r.world * B * 10 / (ms / 1e3), 1), "ms_per_batch": round(ms / 10, 3)}
+        if tag == "ours":
+            # the same forward replayed from one CUDA graph (autocast weight cache off)
+            def fwd_nc(net=net):
+                with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
+                    net(x, t, y)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fwd_nc()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fwd_nc()
+            for _ in range(3):
+                graph.replay()
+            gms = _timed(graph.replay, 10, stream)
+            leg[tag] = {"images_per_s": round(r.world * B * 10 / (gms / 1e3), 1), "ms_per_batch": round(gms / 10, 3),
+                        "path": "one CUDA graph per batch", "eager": leg[tag]}
+            del graph
     out["forward"] = {"config": "BASELINE config 3: B=64 per GPU, bf16 autocast", "batch_per_gpu": B,
                       "steps": 10, **leg.pop("ours"), **({"reference_gpu": leg["reference"]} if leg else {})}
 
