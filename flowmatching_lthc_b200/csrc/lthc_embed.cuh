@@ -267,20 +267,26 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) patch_embed_read_kernel(cons
 
     // ---- epilogue 2: X0 = bf16(D2 + b2) into the staging boxes (row m_R, channels 128 * hf .. + 128)
     if (ok) {
+      // two 32-column loads in flight per wait (the TMEM load latency is paid twice
+      // per tile instead of four times)
 #pragma unroll
-      for (int q32 = 0; q32 < 4; ++q32) {
-        float v[32];
-        const int nb = 128 * hf + 32 * q32;  // first channel of these 32 within the chunk
-        tmem_ld32(tmem_d2 + (static_cast<uint32_t>(32 * lq) << 16) + nb, v);
+      for (int q64 = 0; q64 < 2; ++q64) {
+        uint32_t raw[2][32];
+        tmem_ld32_async(tmem_d2 + (static_cast<uint32_t>(32 * lq) << 16) + 128 * hf + 64 * q64, raw[0]);
+        tmem_ld32_async(tmem_d2 + (static_cast<uint32_t>(32 * lq) << 16) + 128 * hf + 64 * q64 + 32, raw[1]);
+        tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int n = nb + 8 * q;
+        for (int qq = 0; qq < 8; ++qq) {
+          const int n = 128 * hf + 64 * q64 + 8 * qq;  // first of these 8 channels within the chunk
+          float v8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v8[i] = __uint_as_float(raw[qq >> 2][8 * (qq & 3) + i]);
           // the convolution output is rounded to bf16, then the bias is added and
           // the sum rounded again (the reference adds the bias as a separate op)
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 conv = bf16_round2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+            const float2 conv = bf16_round2(v8[2 * e], v8[2 * e + 1]);
             const float2 bb = *reinterpret_cast<const float2*>(bias_s + n + 2 * e);
             const __nv_bfloat162 t = __floats2bfloat162_rn(__fadd_rn(conv.x, bb.x), __fadd_rn(conv.y, bb.y));
             o[e] = *reinterpret_cast<const uint32_t*>(&t);
