@@ -116,7 +116,7 @@ struct FinalSmem {
     tile_bytes = static_cast<size_t>(tile) * C * es;
     const size_t tiles = static_cast<size_t>(stages) * (bwd ? 2 : 1) * tile_bytes;
     consts = tiles;                                    // w, 1 + scale, shift: fp32 [C] each
-    r = consts + 3 * static_cast<size_t>(C) * 4;       // r, grad of the squares: fp32 [2][tile] each
+    r = consts + 3 * static_cast<size_t>(C) * 4;       // r, 2 x grad of the squares: fp32 [2][tile] each
     bars = (r + 4 * static_cast<size_t>(tile) * 4 + 7) & ~static_cast<size_t>(7);
     total = bars + static_cast<size_t>(stages) * 8;
   }
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
   float* sh_s = w_s + C;
   T* s1_s = reinterpret_cast<T*>(sh_s + C);  // 1 + scale, rounded to the dtype
   float* r_s = reinterpret_cast<float*>(smem + plan.r);
-  float* gsq_s = r_s + 2 * p.tile;
+  float* gsq_s = r_s + 2 * p.tile;  // backward: 2 x grad of the squares
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bars);
 
   const int64_t b = blockIdx.y;
@@ -208,7 +208,6 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
   const float2 wv = own ? *reinterpret_cast<const float2*>(w_s + c) : make_float2(0.f, 0.f);
   const float2 shv = own ? *reinterpret_cast<const float2*>(sh_s + c) : make_float2(0.f, 0.f);
   const R s1r = own ? ld_pair<T>(s1_s + c) : P2::rn(make_float2(0.f, 0.f));
-  const float2 two = make_float2(2.f, 2.f);
   float2 aw = make_float2(0.f, 0.f), ash = aw, asc = aw;
 
   auto tile_rows = [&](int i) -> int {
@@ -247,15 +246,16 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
             if (cc < C) {
               const float2 gn = P2::f(P2::mul(ld_pair<T>(gs + k * C + cc), ld_pair<T>(s1_s + cc)));
               const float2 gt = fmul2(gn, *reinterpret_cast<const float2*>(w_s + cc));
-              d2 = fadd2(d2, fmul2(gt, v[j][e]));
+              d2 = ffma2(gt, v[j][e], d2);
             }
           }
         float dot = __fadd_rn(d2.x, d2.y);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
-        // d/dr of rsqrt: -0.5 * g * r^3; mean backward: / C; square backward: * 2x (phase 2)
+        // d/dr of rsqrt: -0.5 * g * r^3; mean backward: / C; square backward: * 2 here
+        // (exact) and * x in phase 2, since (2 gsq) x equals gsq (2 x) in one rounding
         const float gv = __fmul_rn(__fmul_rn(-0.5f, dot), __fmul_rn(__fmul_rn(r, r), r));
-        gsq = __fdiv_rn(gv, p.c_f);
+        gsq = 2.f * __fdiv_rn(gv, p.c_f);
       }
       if (lane == 0) {
         rb[k] = r;
@@ -288,9 +288,9 @@ __global__ void __launch_bounds__(kFinalMaxThreads) final_norm_modulate_kernel(c
         const float2 gn = P2::f(P2::mul(gr, s1r));
         ash = fadd2(ash, gm);
         asc = fadd2(asc, P2::f(P2::mul(gr, nr)));
-        aw = fadd2(aw, fmul2(gn, tt));
+        aw = ffma2(gn, tt, aw);
         const float2 gt = fmul2(gn, wv);
-        *dst = P2::rn(fadd2(fmul2(gt, make_float2(r, r)), fmul2(make_float2(gsq, gsq), fmul2(two, xv))));
+        *dst = P2::rn(fadd2(fmul2(gt, make_float2(r, r)), fmul2(make_float2(gsq, gsq), xv)));
       }
     }
     fence_proxy_async_smem();  // the tile's bulk store reads these writes
