@@ -378,7 +378,10 @@ int broadcast(const void* base, const void* const* dz, const void* const* w, int
 #define LTHC_MATBWD_TC 1  // 0: every materialisation backward runs the CUDA-core read-family kernel
 #endif
 #ifndef LTHC_MATBWD_DZ_STAGES
-#define LTHC_MATBWD_DZ_STAGES 2
+#define LTHC_MATBWD_DZ_STAGES 2  // dz ring of the plan (the smallest shared memory a call may need)
+#endif
+#ifndef LTHC_MATBWD_DZ_STAGES_WGRAD
+#define LTHC_MATBWD_DZ_STAGES_WGRAD 3  // dz ring of a call that forms the weight gradient
 #endif
 
 // Launch plan of matbwd_tc_kernel; ok = false when the shape or dtype is not one
@@ -466,8 +469,24 @@ int matbwd_tc_t(const MbPlan& m, const void* grad_out, const void* const* dz, co
   p.G = static_cast<int>(G);
   p.Gq = m.Gq;
   p.Rq = m.Rq;
-  p.gstages = m.gstages;
-  p.dstages = m.dstages;
+  // ring depths of this call: with the weight gradient a deeper dz ring (the dz
+  // copies are the slower stream), without it no dz ring and a deeper grad X_L ring
+  {
+    const size_t dzb = static_cast<size_t>(L) * kMbDzLayerBytes;
+    const size_t fixed = m.smem - m.dstages * dzb - m.gstages * kMbGxBytes;
+    const size_t budget = 227 * 1024;
+    const int dst = wgrad ? LTHC_MATBWD_DZ_STAGES_WGRAD : 1;
+    const int gst = static_cast<int>(std::min<size_t>(kMbMaxStages, (budget - fixed - dst * dzb) / kMbGxBytes));
+    if (gst >= 2 && fixed + dst * dzb <= budget) {
+      p.gstages = gst;
+      p.dstages = dst;
+    } else {
+      p.gstages = m.gstages;
+      p.dstages = m.dstages;
+    }
+  }
+  const size_t smem = (m.smem - m.dstages * static_cast<size_t>(L) * kMbDzLayerBytes - m.gstages * kMbGxBytes) +
+                      p.dstages * static_cast<size_t>(L) * kMbDzLayerBytes + p.gstages * kMbGxBytes;
   p.need_pool = grad_dz != nullptr;
   p.need_wgrad = wgrad;
   p.visits = m.visits;
@@ -476,9 +495,9 @@ int matbwd_tc_t(const MbPlan& m, const void* grad_out, const void* const* dz, co
   p.Tc = m.Tc;
   p.parts = m.parts;
   int per_sm = 0;
-  LTHC_TRY(resident_ctas(matbwd_tc_kernel<T>, kMbThreads, static_cast<int>(m.smem), &per_sm));
+  LTHC_TRY(resident_ctas(matbwd_tc_kernel<T>, kMbThreads, static_cast<int>(smem), &per_sm));
   if (per_sm < 1) return fail(LTHC_ERR_LAUNCH, "the tensor-core backward does not fit on an SM");
-  matbwd_tc_kernel<T><<<static_cast<unsigned>(m.grid), kMbThreads, m.smem, s>>>(p);
+  matbwd_tc_kernel<T><<<static_cast<unsigned>(m.grid), kMbThreads, smem, s>>>(p);
   LTHC_TRY(launched("materialisation backward (tensor cores)"));
   if (wgrad) {
     const int64_t n = static_cast<int64_t>(L) * C * kPos;

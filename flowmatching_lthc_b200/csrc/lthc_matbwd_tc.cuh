@@ -11,9 +11,11 @@
 // CTAs that run together read every slice of the same cell rows (whole rows of
 // the residual; slice-major order left each DRAM page touched 32 bytes at a
 // time and ran at half the speed).  Each tile arrives as four stages of 32
-// cells: grad X_L by TMA into a 3-slot ring that the transposers release, dz by
-// cp.async into a 2-slot ring that GEMM 2 releases (measured faster than
-// 32-byte-row TMA boxes for dz, and it keeps the TMA engine for grad X_L).
+// cells: grad X_L by TMA into a ring that the transposers release, dz by
+// cp.async into a ring that GEMM 2 releases (measured faster than 32-byte-row
+// TMA boxes for dz, and it keeps the TMA engine for grad X_L).  The host sizes
+// the rings per call: with the weight gradient 3 dz slots and what shared memory
+// leaves for grad X_L (2 slots at L = 12), without it grad X_L alone (4 slots).
 // grad X_L is transposed in shared memory (ldmatrix.trans + stmatrix) into one
 // of two buffers (tile parity)
 //   T[channel half][position half][8 channels][cell][8 positions]   (16-bit, no swizzle)
