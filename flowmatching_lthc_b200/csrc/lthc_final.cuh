@@ -11,9 +11,10 @@
 // to the activation dtype; 1 + scale, the product and the sum each rounded to
 // the activation dtype (torch evaluates 16-bit elementwise ops in fp32 and
 // rounds once per op).  Products and sums use explicit round-to-nearest
-// intrinsics so that no FMA contraction changes a rounding.  Only the order of
-// the two sums over channels (mean of squares; the backward's dot product)
-// differs from torch's reduction tree.
+// intrinsics so that no FMA contraction changes a rounding.  Only the sums
+// differ from torch: the two sums over channels (mean of squares; the
+// backward's dot product) run in another order, and the backward's dot product
+// and its grad-weight sum over tokens are fused multiply-adds.
 //
 // Mapping: a CTA owns a contiguous token range of one image (so the image's
 // shift / scale / weight rows are read once per CTA) and walks it in tiles of
